@@ -1,0 +1,381 @@
+"""Benchmark of the batched AVBD environment step.
+
+Workload: the seed-0 synthetic biped, 4096 environments per GPU, dt 5 ms,
+4 substeps per control step, 10 AVBD iterations, fp32, PD targets HOME +
+N(0, 0.05 rad) drawn once per environment, no self-contact, kp 20 N m/rad,
+torque cap 2 N m.  200 control steps settle the robots (untimed), then W
+warm-up steps, then K timed steps.  One step = one `CudaBatch.step` call = one
+kernel launch advancing every environment 4 physics steps.
+
+Metric: physics env-steps/s = envs x substeps x K / device seconds (the
+reference's formula, scripts/benchmark_engines.py:551), summed over ranks and
+divided by the slowest rank's time.  The L2 cache is flushed (256 MiB write)
+between timed steps, outside the timed events.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ENVS = 4096
+SUBSTEPS = 4
+ITERATIONS = 10
+DT = 0.005
+SETTLE = 200
+NOISE = 0.05
+METRIC = "physics env-steps/s"
+UNIT = "env-steps/s"
+
+
+def workload(args):
+    return {
+        "workload": "config 2: synthetic biped (seed 0), fixed HOME + N(0,0.05 rad) PD targets, ground contact only",
+        "envs_per_gpu": args.envs,
+        "substeps_per_step": SUBSTEPS,
+        "iterations": ITERATIONS,
+        "dt": DT,
+        "settle_steps": SETTLE,
+        "kp": None,
+        "torque_limit": None,
+        "l2": "flushed between timed steps (256 MiB write, outside the timed events)",
+        "parallelism": f"env shards x{args.gpus}, no physics communication",
+    }
+
+
+def make_model(directory, seed=0):
+    from duck_gym_b200 import biped
+
+    path = biped.write(directory, seed=seed)
+    meta = json.loads((Path(directory) / "metadata.json").read_text())
+    return path, meta
+
+
+def fixed_targets(meta, envs, seed):
+    rng = np.random.default_rng(seed)
+    home = np.asarray(meta["home"], np.float32)
+    return (home + rng.normal(0, NOISE, (envs, home.size))).astype(np.float32)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples taken while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        sm, reasons, sm_max, power = [], set(), None, []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": sm_max, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+def count_flops(model, meta, envs, steps):
+    """Algorithmic flops per physics env-step, counted by the CPU oracle's
+    counting scalar on the same workload (HOME start, fixed targets)."""
+    from oracle.oracle import count_ops
+
+    targets = np.repeat(fixed_targets(meta, envs, 0)[None], steps, axis=0)
+    c = count_ops(model, np.asarray(meta["home"], np.float32), targets, np.zeros((envs, 3), np.float32), DT,
+                  ITERATIONS, SUBSTEPS, meta["kp"], meta["torque_limit"])
+    flops = c["add"] + c["mul"] + c["div"] + c["sqrt"]
+    transcendental = c["sin"] + c["cos"] + c["tan"] + c["atan2"] + c["hypot"] + c["remainder"]
+    n = c["physics_steps"]
+    return {"flops_per_env_step": flops / n, "transcendentals_per_env_step": transcendental / n,
+            "gs_iterations_per_env_step": c["gs_iterations"] / n, "sample": f"{envs} envs x {steps} control steps"}
+
+
+def cpu_baseline(model, meta, seconds=15.0):
+    """The reference's own CPU solver (oracle/_ref CpuBatch32) on this host's
+    cores, else the CPU restatement; bounded to about `seconds` of work."""
+    from oracle.oracle import OracleBatch, reference_module
+
+    ref = reference_module()
+    cores = min(64, os.cpu_count() or 1)
+    envs = 4096
+    kind = "reference" if ref is not None else "port"
+    if ref is not None:
+        batch = ref.CpuBatch32(str(model), envs, DT, ITERATIONS, cores)
+    else:
+        batch = OracleBatch(model, envs, DT, ITERATIONS, threads=cores)
+    target = fixed_targets(meta, envs, 0)
+    forces = np.zeros((envs, 3), np.float32)
+    t0 = time.perf_counter()
+    batch.step(target, forces, SUBSTEPS, meta["kp"], meta["torque_limit"])
+    first = time.perf_counter() - t0
+    steps = max(1, min(200, int(seconds / max(first, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        batch.step(target, forces, SUBSTEPS, meta["kp"], meta["torque_limit"])
+    elapsed = time.perf_counter() - t0
+    return {"value": envs * SUBSTEPS * steps / elapsed, "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{envs} envs x {steps} control steps ({SUBSTEPS} substeps), after 1 untimed step, wall clock"}
+
+
+def traffic_from_profile():
+    """DRAM bytes per advance launch from the committed ncu summary, if any."""
+    path = ROOT / "profiles" / "advance_biped4096.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1])
+            except ValueError:
+                return None
+    return None
+
+
+def reference_arm(args, rank, world):
+    """--impl reference: the reference's CPU solver (oracle/_ref, else the
+    oracle port) on the host cores, same workload and metric."""
+    if rank != 0:
+        return
+    with tempfile.TemporaryDirectory() as d:
+        model, meta = make_model(d)
+        from oracle.oracle import OracleBatch, reference_module
+
+        ref = reference_module()
+        cores = min(64, os.cpu_count() or 1)
+        envs = min(args.envs, 4096)
+        kind = "reference" if ref is not None else "port"
+        if ref is not None:
+            batch = ref.CpuBatch32(str(model), envs, DT, ITERATIONS, cores)
+        else:
+            batch = OracleBatch(model, envs, DT, ITERATIONS, threads=cores)
+        target = fixed_targets(meta, envs, 0)
+        forces = np.zeros((envs, 3), np.float32)
+        for _ in range(args.warmup):
+            batch.step(target, forces, SUBSTEPS, meta["kp"], meta["torque_limit"])
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            batch.step(target, forces, SUBSTEPS, meta["kp"], meta["torque_limit"])
+        elapsed = time.perf_counter() - t0
+        value = envs * SUBSTEPS * args.steps / elapsed
+        cfg = workload(args)
+        cfg.update(kp=meta["kp"], torque_limit=meta["torque_limit"], envs_per_gpu=envs,
+                   settle_steps=0, l2="host run")
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * elapsed / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
+                             "sample": f"{envs} envs x {args.steps} control steps after {args.warmup} warm-up"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--envs", type=int, default=ENVS)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    args = p.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    from duck_gym_b200 import CudaBatch, fp32_peak_tflops
+
+    with tempfile.TemporaryDirectory() as d:
+        model, meta = make_model(d)
+        kp, limit = meta["kp"], meta["torque_limit"]
+        envs = args.envs
+        batch = CudaBatch(model, envs, DT, ITERATIONS, local)
+        target_host = fixed_targets(meta, envs, 1000 * rank)
+        target = torch.from_numpy(target_host).to(device)
+        forces = torch.zeros(envs, 3, device=device)
+        for _ in range(SETTLE):
+            batch.step(target, forces, SUBSTEPS, kp, limit)
+        for _ in range(args.warmup):
+            batch.step(target, forces, SUBSTEPS, kp, limit)
+        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)  # 256 MiB > L2
+        stream = torch.cuda.current_stream(device)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+
+        def barrier():
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(device)
+
+        launches0 = batch.launches
+        barrier()
+        with ClockSampler(local) as clocks:
+            wall0 = time.perf_counter()
+            for k in range(args.steps):
+                flush.zero_()
+                starts[k].record(stream)
+                batch.step(target, forces, SUBSTEPS, kp, limit)
+                ends[k].record(stream)
+            barrier()
+            wall = time.perf_counter() - wall0
+        launches = batch.launches - launches0
+        kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        device_s = sum(kernel_ms) / 1e3
+        t = torch.tensor([device_s], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        slowest = float(t.item())
+        total_steps = envs * SUBSTEPS * args.steps * world
+        value = total_steps / slowest
+
+        # End to end through the public API: pinned host targets in, one
+        # step, state() snapshot, diagnostics back to the host, every step.
+        host_in = torch.from_numpy(target_host).pin_memory()
+        host_forces = torch.zeros(envs, 3).pin_memory()
+        host_out = torch.empty(envs, 6).pin_memory()
+        e2e_steps = max(10, args.steps // 2)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            tin = host_in.to(device, non_blocking=True)
+            fin = host_forces.to(device, non_blocking=True)
+            batch.step(tin, fin, SUBSTEPS, kp, limit)
+            diag = batch.state()[2]
+            host_out.copy_(diag, non_blocking=True)
+        e1.record(stream)
+        barrier()
+        e2e_s = torch.tensor([e0.elapsed_time(e1) / 1e3], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+        e2e_value = envs * SUBSTEPS * e2e_steps * world / float(e2e_s.item())
+        failed_fraction = float((host_out[:, 5] > 0).float().mean())
+
+        line = None
+        if rank == 0:
+            peak = fp32_peak_tflops(local)
+            flops = count_flops(model, meta, 64, 50)
+            mean_kernel_s = statistics.mean(kernel_ms) / 1e3
+            achieved = flops["flops_per_env_step"] * envs * SUBSTEPS / mean_kernel_s / 1e12
+            state_bytes = batch.record_length * 4  # record read + written per launch (upper bound)
+            hbm_algorithmic = envs * (2 * state_bytes) + envs * (14 + 3) * 4
+            peaks = {}
+            peaks_path = ROOT / "MEASURED_PEAKS.json"
+            if peaks_path.exists():
+                peaks = json.loads(peaks_path.read_text())
+            hbm_peak = peaks.get("hbm_gbs", 6650.0)
+            traffic = traffic_from_profile()
+            cfg = workload(args)
+            cfg.update(kp=kp, torque_limit=limit)
+            line = {
+                "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1e3 * slowest / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded biped, no dataset)",
+                "config": cfg,
+                "roofline": {
+                    "bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                    "traffic": traffic,
+                    "kernel": "advanceKernel<float,8>",
+                    "peak_source": "measured: FP32 FMA probe on this GPU (duck_fp32_peak), 2 flops per FMA",
+                    "flops_per_env_step": flops["flops_per_env_step"],
+                    "flops_source": "oracle counting scalar (+,-,*,/,sqrt), " + flops["sample"],
+                    "transcendentals_per_env_step": flops["transcendentals_per_env_step"],
+                    "hbm": {"algorithmic_bytes_per_launch": hbm_algorithmic,
+                            "achieved_gbs": hbm_algorithmic / mean_kernel_s / 1e9, "peak_gbs": hbm_peak,
+                            "frac": hbm_algorithmic / mean_kernel_s / 1e9 / hbm_peak,
+                            "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650 GB/s"},
+                },
+                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": envs * (14 + 3) * 4,
+                        "d2h_bytes_per_step": envs * 6 * 4,
+                        "path": "CudaBatch.step + CudaBatch.state() with pinned host targets/forces in and diag out"},
+                "gpu_launches": launches,
+                "clocks": clocks.summary(),
+                "wall_s": wall,
+                "failed_env_fraction": failed_fraction,
+            }
+            if not args.no_cpu_baseline and world == 1:
+                line["cpu_baseline"] = cpu_baseline(model, meta)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        if line is not None:
+            print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,261 @@
+// Kernels around the hot step: initialise/reset, state snapshot, contact
+// force / count / self-contact statistics, hinge generalized loads, and the
+// FP32 throughput probe.  All read and write the portable per-env records.
+#pragma once
+#include "solver.cuh"
+
+namespace duckb200 {
+
+template <class R> __device__ __forceinline__ V3<R> gv3(const R *p) { return {p[0], p[1], p[2]}; }
+template <class R> __device__ __forceinline__ Q4<R> gq4(const R *p) { return {p[0], p[1], p[2], p[3]}; }
+template <class R> __device__ __forceinline__ void sv3(R *p, V3<R> v) { p[0] = v.x; p[1] = v.y; p[2] = v.z; }
+template <class R> __device__ __forceinline__ void sq4(R *p, Q4<R> q) { p[0] = q.w; p[1] = q.x; p[2] = q.y; p[3] = q.z; }
+template <class R> __device__ __forceinline__ V3<R> mvec(const R (&a)[3]) { return {__ldg(&a[0]), __ldg(&a[1]), __ldg(&a[2])}; }
+template <class R> __device__ __forceinline__ Q4<R> mquat(const R (&a)[4]) {
+  return {__ldg(&a[0]), __ldg(&a[1]), __ldg(&a[2]), __ldg(&a[3])};
+}
+
+// BasicState::initialize + resetPose (kernel.cuh:383-420; extension.cu:22-50),
+// one thread per environment.  pose == 0 initialises without a pose offset.
+template <class R>
+__global__ void resetKernel(const DevModel<R> *__restrict__ m, R *records, int stride, int count,
+                            const uint8_t *mask, const R *q, const R *roots, int pose) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= count || (mask && !mask[e])) return;
+  R *rec = records + size_t(e) * stride;
+  const int nb = m->nb, nj = m->nj;
+  if (pose) {
+    for (int k = 0; k < 6; ++k)
+      if (!isfinite(roots[6 * size_t(e) + k])) { rec[0] = R(1); return; }
+    for (int k = 0; k < nj; ++k)
+      if (!isfinite(q[size_t(e) * nj + k])) { rec[0] = R(1); return; }
+  }
+  for (int k = 0; k < kRecHeader; ++k) rec[k] = R(0);
+  R *bodies = rec + kRecHeader;
+  for (int b = 0; b < nb; ++b) {
+    R *r = bodies + kRecBody * b;
+    sv3(r, mvec(m->x[b]));
+    sq4(r + 3, mquat(m->q[b]));
+    sv3(r + 7, mvec(m->v[b]));
+    sv3(r + 10, mvec(m->w[b]));
+    r[13] = r[14] = r[15] = R(0);
+  }
+  R *joints = bodies + kRecBody * nb;
+  for (int j = 0; j < nj; ++j) {
+    R *r = joints + kRecJoint * j;
+    for (int k = 0; k < 7; ++k) { r[k] = R(0); r[7 + k] = k < 3 ? R(1000) : R(1); }
+    r[14] = R(0); r[15] = R(1);
+    r[16] = __ldg(&m->target[j]); r[17] = __ldg(&m->kp[j]); r[18] = __ldg(&m->maxTorque[j]);
+    r[19] = __ldg(&m->torque[j]); r[20] = __ldg(&m->frictionloss[j]); r[21] = __ldg(&m->damping[j]);
+  }
+  if (!pose) return;
+  const R *root = roots + 6 * size_t(e);
+  const R *qe = q + size_t(e) * nj;
+  for (int b = 0; b < nb; ++b) { bodies[kRecBody * b + 7] = bodies[kRecBody * b + 8] = bodies[kRecBody * b + 9] = R(0);
+    bodies[kRecBody * b + 10] = bodies[kRecBody * b + 11] = bodies[kRecBody * b + 12] = R(0); }
+  R *base = bodies + kRecBody * 1;
+  sv3(base, gv3(base) + V3<R>{root[0], root[1], root[2]});
+  sq4(base + 3, qmul(qexp(V3<R>{root[3], root[4], root[5]}), gq4(base + 3)));
+  for (int j = 0; j < nj; ++j) {
+    const int a = __ldg(&m->ja[j]), b = __ldg(&m->jb[j]);
+    const Q4<R> oa = mquat(m->q[a]), ob = mquat(m->q[b]);
+    V3<R> oaxis = rotate(oa, mvec(m->axisA[j])), t = rotate(oa, mvec(m->tangentA[j])),
+          u = rotate(ob, mvec(m->tangentB[j]));
+    R original = atan2(dot(oaxis, cross(t, u)), dot(t, u));
+    R *ra = bodies + kRecBody * a, *rb = bodies + kRecBody * b;
+    Q4<R> qa = gq4(ra + 3);
+    V3<R> axis = rotate(qa, mvec(m->axisA[j]));
+    Q4<R> qb = qnormalized(qmul(qmul(qmul(qexp(axis * (qe[j] - original)), qa), conj(oa)), ob));
+    sq4(rb + 3, qb);
+    sv3(rb, gv3(ra) + rotate(qa, mvec(m->ra[j])) - rotate(qb, mvec(m->rb[j])));
+  }
+}
+
+// Hinge angle and rate from a record (kernel.cuh:725-731, 563-568).
+template <class R>
+__device__ __forceinline__ void jointState(const DevModel<R> *m, const R *bodies, int j, R *angle, R *rate) {
+  const int a = __ldg(&m->ja[j]), b = __ldg(&m->jb[j]);
+  Q4<R> qa = gq4(bodies + kRecBody * a + 3), qb = gq4(bodies + kRecBody * b + 3);
+  V3<R> axis = rotate(qa, mvec(m->axisA[j])), t = rotate(qa, mvec(m->tangentA[j])),
+        u = rotate(qb, mvec(m->tangentB[j]));
+  *angle = atan2(dot(axis, cross(t, u)), dot(t, u));
+  *rate = dot(gv3(bodies + kRecBody * b + 10) - gv3(bodies + kRecBody * a + 10), axis);
+}
+
+// BasicState::snapshot (kernel.cuh:555-575): one thread per (env, body),
+// (env, joint) or (env, diagnostics row), so the outputs are written densely.
+template <class R>
+__global__ void snapshotKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
+                               R *bodiesOut, R *jointsOut, R *diagOut) {
+  const int nb = m->nb, nj = m->nj, items = nb + nj + 1;
+  const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (t >= (long long)count * items) return;
+  const int e = int(t / items), item = int(t % items);
+  const R *rec = records + size_t(e) * stride;
+  const R *bodies = rec + kRecHeader;
+  if (item < nb) {
+    const R *r = bodies + kRecBody * item;
+    R *o = bodiesOut + (size_t(e) * nb + item) * 13;
+    for (int k = 0; k < 13; ++k) o[k] = r[k];
+  } else if (item < nb + nj) {
+    const int j = item - nb;
+    R angle, rate;
+    jointState(m, bodies, j, &angle, &rate);
+    jointsOut[(size_t(e) * nj + j) * 2] = angle;
+    jointsOut[(size_t(e) * nj + j) * 2 + 1] = rate;
+  } else {
+    R *o = diagOut + size_t(e) * 6;
+    o[0] = rec[2]; o[1] = rec[3]; o[2] = rec[4]; o[3] = rec[5]; o[4] = rec[6]; o[5] = rec[0];
+  }
+}
+
+template <class R> __device__ __forceinline__ const R *recContacts(const DevModel<R> *m, const R *rec) {
+  return rec + kRecHeader + kRecBody * m->nb + kRecJoint * m->nj;
+}
+template <class R> __device__ __forceinline__ V3<R> recContactWorld(const R *c, V3<R> v) {
+  return V3<R>{c[15], c[16], c[17]} * v.x + V3<R>{c[18], c[19], c[20]} * v.y + V3<R>{c[21], c[22], c[23]} * v.z;
+}
+
+// BasicState::contactForces (kernel.cuh:467-480), one thread per environment.
+template <class R>
+__global__ void contactForcesKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
+                                    R *out, int groundOnly) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= count) return;
+  const int nb = m->nb;
+  R *o = out + size_t(e) * nb * 3;
+  for (int i = 0; i < nb * 3; ++i) o[i] = R(0);
+  const R *rec = records + size_t(e) * stride;
+  const R *cs = recContacts(m, rec);
+  const int n = int(rec[1]);
+  for (int i = 0; i < n; ++i) {
+    const R *c = cs + kRecContact * i;
+    const int body = int(c[0]), other = int(c[3]);
+    if (groundOnly && other >= 0) continue;
+    V3<R> f = -recContactWorld(c, V3<R>{c[26], c[27], c[28]});
+    o[3 * body] += f.x; o[3 * body + 1] += f.y; o[3 * body + 2] += f.z;
+    if (other >= 0) { o[3 * other] -= f.x; o[3 * other + 1] -= f.y; o[3 * other + 2] -= f.z; }
+  }
+}
+
+// contactCounts / selfContactStats (kernel.cuh:481-498).
+template <class R>
+__global__ void contactStatsKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
+                                   R *counts, R *selfStats) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= count) return;
+  const R *rec = records + size_t(e) * stride;
+  const R *bodies = rec + kRecHeader;
+  const R *cs = recContacts(m, rec);
+  const int n = int(rec[1]);
+  R ground = R(0), self = R(0), active = R(0), depthMax = R(0);
+  for (int i = 0; i < n; ++i) {
+    const R *c = cs + kRecContact * i;
+    const int body = int(c[0]), other = int(c[3]);
+    if (other < 0) { ground += R(1); continue; }
+    self += R(1);
+    if (!selfStats) continue;
+    V3<R> ra = rotate(gq4(bodies + kRecBody * body + 3), V3<R>{c[6], c[7], c[8]});
+    V3<R> rb = rotate(gq4(bodies + kRecBody * other + 3), V3<R>{c[12], c[13], c[14]});
+    V3<R> delta = gv3(bodies + kRecBody * body) + ra - gv3(bodies + kRecBody * other) - rb;
+    R gapN = dot(delta, V3<R>{c[21], c[22], c[23]});
+    R depth = rmax(R(0), -gapN);
+    if (c[28] < R(-1e-5) || depth > R(1e-6)) active += R(1);
+    depthMax = rmax(depthMax, depth);
+  }
+  if (counts) { counts[2 * size_t(e)] = ground; counts[2 * size_t(e) + 1] = self; }
+  if (selfStats) { selfStats[2 * size_t(e)] = active; selfStats[2 * size_t(e) + 1] = depthMax; }
+}
+
+// BasicState::generalizedLoads (kernel.cuh:504-554): RNEA at zero joint
+// acceleration, one thread per environment.
+template <class R>
+__global__ void generalizedLoadsKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
+                                       const R *offset, R *out) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= count) return;
+  const int nb = m->nb, nj = m->nj;
+  const R *rec = records + size_t(e) * stride;
+  const R *bodies = rec + kRecHeader;
+  const R *joints = bodies + kRecBody * nb;
+  V3<R> acc[kMaxBodies], alpha[kMaxBodies], force[kMaxBodies], moment[kMaxBodies], contact[kMaxBodies],
+      contactMoment[kMaxBodies];
+  const V3<R> zero{R(0), R(0), R(0)};
+  for (int b = 0; b < nb; ++b) acc[b] = alpha[b] = force[b] = moment[b] = contact[b] = contactMoment[b] = zero;
+  auto X = [&](int b) { return gv3(bodies + kRecBody * b); };
+  auto Q = [&](int b) { return gq4(bodies + kRecBody * b + 3); };
+  auto W = [&](int b) { return gv3(bodies + kRecBody * b + 10); };
+  const R *off = offset + 3 * size_t(e);
+  acc[1] = cross(W(1), cross(W(1), rotate(Q(1), V3<R>{off[0], off[1], off[2]})));
+  for (int j = 0; j < nj; ++j) {
+    const int a = __ldg(&m->ja[j]), b = __ldg(&m->jb[j]);
+    V3<R> axis = rotate(Q(a), mvec(m->axisA[j])), ra = rotate(Q(a), mvec(m->ra[j])), rb = rotate(Q(b), mvec(m->rb[j]));
+    R speed = dot(W(b) - W(a), axis);
+    alpha[b] = alpha[a] + cross(W(a), axis) * speed;
+    acc[b] = acc[a] + cross(alpha[a], ra) + cross(W(a), cross(W(a), ra)) - cross(alpha[b], rb) - cross(W(b), cross(W(b), rb));
+  }
+  const V3<R> gravity{m->gravity[0], m->gravity[1], m->gravity[2]};
+  for (int i = 1; i < nb; ++i) {
+    const R mass = __ldg(&m->mass[i]);
+    const V3<R> in = mvec(m->inertia[i]);
+    const Q4<R> q = Q(i);
+    auto inertiaMul = [&](V3<R> v) {
+      V3<R> l = rotateInv(q, v);
+      return rotate(q, V3<R>{l.x * in.x, l.y * in.y, l.z * in.z});
+    };
+    force[i] = (acc[i] - gravity) * mass;
+    moment[i] = inertiaMul(alpha[i]) + cross(W(i), inertiaMul(W(i)));
+  }
+  const R *cs = recContacts(m, rec);
+  const int n = int(rec[1]);
+  for (int i = 0; i < n; ++i) {
+    const R *c = cs + kRecContact * i;
+    const int body = int(c[0]), other = int(c[3]);
+    V3<R> f = -recContactWorld(c, V3<R>{c[26], c[27], c[28]});
+    contact[body] = contact[body] + f;
+    contactMoment[body] = contactMoment[body] + cross(rotate(Q(body), V3<R>{c[6], c[7], c[8]}), f);
+    if (other >= 0) {
+      contact[other] = contact[other] - f;
+      contactMoment[other] = contactMoment[other] + cross(rotate(Q(other), V3<R>{c[12], c[13], c[14]}), -f);
+    }
+  }
+  R *o = out + size_t(e) * nj * 3;
+  for (int k = nj - 1; k >= 0; --k) {
+    const int a = __ldg(&m->ja[k]), b = __ldg(&m->jb[k]);
+    const R *jr = joints + kRecJoint * k;
+    V3<R> axis = rotate(Q(a), mvec(m->axisA[k])), rb = rotate(Q(b), mvec(m->rb[k])), shift = X(b) - X(a);
+    o[3 * k] = dot(axis, moment[b] - cross(rb, force[b]));
+    o[3 * k + 1] = dot(axis, contactMoment[b] - cross(rb, contact[b])) +
+                   (__ldg(&m->limited[k]) ? -jr[5] + jr[6] : R(0));
+    R angle, rate;
+    jointState(m, bodies, k, &angle, &rate);
+    const R kp = jr[17], maxTorque = jr[18];
+    R motor = jr[19] - kp * wrapAngle(angle - jr[16]);
+    o[3 * k + 2] = maxTorque > R(0) ? rclamp(motor, -maxTorque, maxTorque) : motor;
+    moment[a] = moment[a] + (moment[b] + cross(shift, force[b]));
+    force[a] = force[a] + force[b];
+    contactMoment[a] = contactMoment[a] + (contactMoment[b] + cross(shift, contact[b]));
+    contact[a] = contact[a] + contact[b];
+  }
+}
+
+// Validation of the generalized-load offsets happens on the device: a
+// non-finite offset poisons only that environment's output (NaN rows).
+
+// FP32 FMA throughput probe: eight independent chains per thread.
+__global__ void fmaPeakKernel(float *sink, int iterations, float seed) {
+  float a[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] = seed + threadIdx.x * 1e-7f + k;
+  const float b = 0.999999f, c = 1e-7f;
+  for (int i = 0; i < iterations; ++i) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = fmaf(a[k], b, c);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) s += a[k];
+  if (s == 1234.5f) sink[0] = s;
+}
+
+}  // namespace duckb200

@@ -1,0 +1,135 @@
+// Device vector / quaternion algebra for the AVBD kernels.
+//
+// Two families:
+//  * plain operators (V3 + V3, dot, rotate, ...): the compiler may contract
+//    them into FMAs.  Used by the primal/dual solve, whose parity bound is a
+//    tolerance (1e-4 m / rad per substep).
+//  * x-prefixed functions (xadd, xdot, xrotate, ...): every multiply and add
+//    is rounded separately (__fmul_rn / __fadd_rn never contract), in the
+//    same order as the reference's C++ (src/cuda/kernel.cuh:86-160), and the
+//    thresholds compare in double exactly like the reference's implicit
+//    promotions.  Used by contact generation, whose parity bound is bit
+//    equality of the contact sets.
+#pragma once
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+namespace duckb200 {
+
+template <class R> struct V3 { R x, y, z; };
+template <class R> struct Q4 { R w, x, y, z; };
+
+// ---------------------------------------------------------------- scalar ops
+__device__ __forceinline__ float xadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float xsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float xmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ double xadd(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ double xsub(double a, double b) { return __dsub_rn(a, b); }
+__device__ __forceinline__ double xmul(double a, double b) { return __dmul_rn(a, b); }
+
+template <class R> __device__ __forceinline__ R rmin(R a, R b) { return a < b ? a : b; }
+template <class R> __device__ __forceinline__ R rmax(R a, R b) { return a > b ? a : b; }
+template <class R> __device__ __forceinline__ R rclamp(R v, R a, R b) { return rmin(rmax(v, a), b); }
+
+// hypot(float, float) of the reference's host build is correctly rounded; the
+// double evaluation below reproduces it (exact squares, one rounding each for
+// the sum, the root and the final narrowing).
+__device__ __forceinline__ float xhypot(float x, float y) {
+  double dx = x, dy = y;
+  return float(__dsqrt_rn(__dadd_rn(__dmul_rn(dx, dx), __dmul_rn(dy, dy))));
+}
+__device__ __forceinline__ double xhypot(double x, double y) { return hypot(x, y); }
+
+// Approximate square root (PTX sqrt.approx) for stiffness majorizers.
+__device__ __forceinline__ float fsqrt(float x) {
+  float r;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ double fsqrt(double x) { return sqrt(x); }
+
+// ---------------------------------------------------------------- fast V3
+template <class R> __device__ __forceinline__ V3<R> operator+(V3<R> a, V3<R> b) { return {a.x + b.x, a.y + b.y, a.z + b.z}; }
+template <class R> __device__ __forceinline__ V3<R> operator-(V3<R> a, V3<R> b) { return {a.x - b.x, a.y - b.y, a.z - b.z}; }
+template <class R> __device__ __forceinline__ V3<R> operator-(V3<R> a) { return {-a.x, -a.y, -a.z}; }
+template <class R> __device__ __forceinline__ V3<R> operator*(V3<R> a, R s) { return {a.x * s, a.y * s, a.z * s}; }
+template <class R> __device__ __forceinline__ R dot(V3<R> a, V3<R> b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
+template <class R> __device__ __forceinline__ V3<R> cross(V3<R> a, V3<R> b) {
+  return {a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x};
+}
+template <class R> __device__ __forceinline__ R norm(V3<R> a) { return sqrt(dot(a, a)); }
+template <class R> __device__ __forceinline__ R comp(V3<R> a, int k) { return k == 0 ? a.x : (k == 1 ? a.y : a.z); }
+template <class R> __device__ __forceinline__ Q4<R> conj(Q4<R> q) { return {q.w, -q.x, -q.y, -q.z}; }
+template <class R> __device__ __forceinline__ Q4<R> qmul(Q4<R> a, Q4<R> b) {
+  return {a.w * b.w - a.x * b.x - a.y * b.y - a.z * b.z,
+          a.w * b.x + a.x * b.w + a.y * b.z - a.z * b.y,
+          a.w * b.y - a.x * b.z + a.y * b.w + a.z * b.x,
+          a.w * b.z + a.x * b.y - a.y * b.x + a.z * b.w};
+}
+template <class R> __device__ __forceinline__ Q4<R> qnormalized(Q4<R> q) {
+  R n = sqrt(q.w * q.w + q.x * q.x + q.y * q.y + q.z * q.z);
+  if (!(n >= R(1e-15))) return {R(NAN), R(NAN), R(NAN), R(NAN)};
+  R inv = R(1) / n;
+  return {q.w * inv, q.x * inv, q.y * inv, q.z * inv};
+}
+// v + 2 u x (u x v + w v): the reference's rotation (kernel.cuh:132-135).
+template <class R> __device__ __forceinline__ V3<R> rotate(Q4<R> q, V3<R> v) {
+  V3<R> u{q.x, q.y, q.z};
+  return v + cross(u, cross(u, v) + v * q.w) * R(2);
+}
+template <class R> __device__ __forceinline__ V3<R> rotateInv(Q4<R> q, V3<R> v) { return rotate(conj(q), v); }
+
+__device__ __forceinline__ void sincosT(float a, float *s, float *c) { sincosf(a, s, c); }
+__device__ __forceinline__ void sincosT(double a, double *s, double *c) { sincos(a, s, c); }
+
+// Exponential map of a rotation vector (kernel.cuh:136-145).
+template <class R> __device__ __forceinline__ Q4<R> qexp(V3<R> v) {
+  R a = norm(v), s, c;
+  sincosT(a * R(0.5), &s, &c);
+  R k = a < R(1e-8) ? R(0.5) - a * a / R(48) : s / a;
+  return qnormalized(Q4<R>{c, k * v.x, k * v.y, k * v.z});
+}
+// Logarithm of a unit quaternion (kernel.cuh:146-153).
+template <class R> __device__ __forceinline__ V3<R> qlog(Q4<R> q) {
+  q = qnormalized(q);
+  if (q.w < R(0)) q = {-q.w, -q.x, -q.y, -q.z};
+  V3<R> v{q.x, q.y, q.z};
+  R s = norm(v);
+  return v * (s < R(1e-10) ? R(2) : R(2) * atan2(s, q.w) / s);
+}
+// remainder(a, 2 pi) as the reference computes it, in double
+// (kernel.cuh:154-160).  Angles already inside (-pi, pi) are returned as is,
+// which is exactly what the double remainder gives for them.
+template <class R> __device__ __forceinline__ R wrapAngle(R a) {
+  const double pi = 3.14159265358979311600;
+  double d = double(a);
+  if (fabs(d) < pi) return a;
+  return R(remainder(d, 2.0 * pi));
+}
+
+// ---------------------------------------------------------------- exact V3
+template <class R> __device__ __forceinline__ V3<R> xadd(V3<R> a, V3<R> b) { return {xadd(a.x, b.x), xadd(a.y, b.y), xadd(a.z, b.z)}; }
+template <class R> __device__ __forceinline__ V3<R> xsub(V3<R> a, V3<R> b) { return {xsub(a.x, b.x), xsub(a.y, b.y), xsub(a.z, b.z)}; }
+template <class R> __device__ __forceinline__ V3<R> xscale(V3<R> a, R s) { return {xmul(a.x, s), xmul(a.y, s), xmul(a.z, s)}; }
+template <class R> __device__ __forceinline__ R xdot(V3<R> a, V3<R> b) {
+  return xadd(xadd(xmul(a.x, b.x), xmul(a.y, b.y)), xmul(a.z, b.z));
+}
+template <class R> __device__ __forceinline__ V3<R> xcross(V3<R> a, V3<R> b) {
+  return {xsub(xmul(a.y, b.z), xmul(a.z, b.y)), xsub(xmul(a.z, b.x), xmul(a.x, b.z)),
+          xsub(xmul(a.x, b.y), xmul(a.y, b.x))};
+}
+template <class R> __device__ __forceinline__ R xnorm(V3<R> a) { return sqrt(xdot(a, a)); }
+// Vec3 / s is a multiplication by the reciprocal in the reference (kernel.cuh:100).
+template <class R> __device__ __forceinline__ V3<R> xdiv(V3<R> a, R s) { return xscale(a, R(1) / s); }
+template <class R> __device__ __forceinline__ V3<R> xunit(V3<R> a) {
+  R n = xnorm(a);
+  if (double(n) < 1e-15) return {R(NAN), R(NAN), R(NAN)};
+  return xdiv(a, n);
+}
+template <class R> __device__ __forceinline__ V3<R> xrotate(Q4<R> q, V3<R> v) {
+  V3<R> u{q.x, q.y, q.z};
+  return xadd(v, xscale(xcross(u, xadd(xcross(u, v), xscale(v, q.w))), R(2)));
+}
+
+}  // namespace duckb200

@@ -1,0 +1,462 @@
+// C ABI of the B200 AVBD library (declared in include/duck_b200.h).
+//
+// A duck_batch owns: the flat device model, the convex point pool, and one
+// portable record per environment (header, bodies, joints, contacts).  Every
+// entry point validates its arguments on the host, orders itself after the
+// batch's previous work with a private event (the reference's wait()/record(),
+// src/cuda/extension.cu:203-205) and launches on the caller's stream.
+#include "../../include/duck_b200.h"
+#include "aux_kernels.cuh"
+
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+using namespace duckb200;
+
+namespace {
+thread_local std::string lastError;
+
+struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+void check(cudaError_t e, const char *what) {
+  if (e != cudaSuccess) throw CudaError(std::string(what) + ": " + cudaGetErrorString(e));
+}
+void require(bool c, const char *msg) {
+  if (!c) throw std::invalid_argument(msg);
+}
+int teamSize(int colorMax) {
+  int t = 4;
+  while (t < colorMax && t < 32) t *= 2;
+  return t;
+}
+}  // namespace
+
+struct duck_batch {
+  int device = 0, fp64 = 0, n = 0, nb = 0, nj = 0, bound = 0, recordLength = 0, recordStride = 0;
+  int T = 8, teamsPerBlock = 4, smemPerBlock = 0;
+  Layout layout{};
+  void *devModel = nullptr, *points = nullptr, *records = nullptr;
+  size_t modelBytes = 0;
+  cudaEvent_t ready = nullptr;
+  std::vector<std::string> names;
+  std::shared_ptr<void> hostModel;  // HostModel<float|double>
+  int64_t launches = 0;
+};
+
+namespace {
+
+template <class R> const HostModel<R> &host(const duck_batch *b) {
+  return *static_cast<const HostModel<R> *>(b->hostModel.get());
+}
+
+struct DeviceGuard {
+  int previous = 0;
+  explicit DeviceGuard(int device) {
+    check(cudaGetDevice(&previous), "cudaGetDevice");
+    check(cudaSetDevice(device), "cudaSetDevice");
+  }
+  ~DeviceGuard() { cudaSetDevice(previous); }
+};
+
+void begin(duck_batch *b, cudaStream_t s) { check(cudaStreamWaitEvent(s, b->ready, 0), "cudaStreamWaitEvent"); }
+void finish(duck_batch *b, cudaStream_t s) {
+  check(cudaGetLastError(), "kernel launch");
+  check(cudaEventRecord(b->ready, s), "cudaEventRecord");
+}
+int blocksFor(long long threads, int per) { return int((threads + per - 1) / per); }
+
+template <class R> void setupAdvance(duck_batch *b) {
+  auto set = [&](auto kernel) {
+    check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, b->smemPerBlock),
+          "cudaFuncSetAttribute");
+  };
+  switch (b->T) {
+    case 4: set(advanceKernel<R, 4>); break;
+    case 8: set(advanceKernel<R, 8>); break;
+    case 16: set(advanceKernel<R, 16>); break;
+    default: set(advanceKernel<R, 32>); break;
+  }
+}
+
+template <class R> void launchAdvance(duck_batch *b, const StepArgs &args, cudaStream_t s) {
+  const int grid = blocksFor(b->n, b->teamsPerBlock);
+  const R *pts = static_cast<const R *>(b->points);
+  const DevModel<R> *m = static_cast<const DevModel<R> *>(b->devModel);
+  R *rec = static_cast<R *>(b->records);
+  switch (b->T) {
+    case 4: advanceKernel<R, 4><<<grid, 32, b->smemPerBlock, s>>>(m, pts, rec, b->recordStride, b->n, b->layout, args); break;
+    case 8: advanceKernel<R, 8><<<grid, 32, b->smemPerBlock, s>>>(m, pts, rec, b->recordStride, b->n, b->layout, args); break;
+    case 16: advanceKernel<R, 16><<<grid, 32, b->smemPerBlock, s>>>(m, pts, rec, b->recordStride, b->n, b->layout, args); break;
+    default: advanceKernel<R, 32><<<grid, 32, b->smemPerBlock, s>>>(m, pts, rec, b->recordStride, b->n, b->layout, args); break;
+  }
+  ++b->launches;
+}
+
+template <class R> void launchReset(duck_batch *b, const uint8_t *mask, const void *q, const void *roots, int pose,
+                                    cudaStream_t s) {
+  resetKernel<R><<<blocksFor(b->n, 128), 128, 0, s>>>(
+      static_cast<const DevModel<R> *>(b->devModel), static_cast<R *>(b->records), b->recordStride, b->n, mask,
+      static_cast<const R *>(q), static_cast<const R *>(roots), pose);
+  ++b->launches;
+}
+
+template <class R> duck_batch *create(const ParsedModel &parsed, int n, double dt, int iterations, int device,
+                                      bool specialized, cudaStream_t s) {
+  auto hm = std::make_shared<HostModel<R>>(convertModel<R>(parsed, dt, iterations, specialized));
+  auto b = std::make_unique<duck_batch>();
+  b->device = device;
+  b->fp64 = std::is_same_v<R, double>;
+  b->n = n;
+  b->nb = hm->dev.nb;
+  b->nj = hm->dev.nj;
+  b->bound = hm->dev.bound;
+  b->names = hm->jointNames;
+  b->recordLength = kRecHeader + kRecBody * b->nb + kRecJoint * b->nj + kRecContact * b->bound;
+  b->recordStride = (b->recordLength + 31) & ~31;
+  b->layout = makeLayout(hm->dev);
+  b->T = teamSize(hm->dev.colorMax);
+  b->teamsPerBlock = 32 / b->T;
+  b->smemPerBlock = int(b->teamsPerBlock * b->layout.size * sizeof(R));
+  int maxShared = 0;
+  check(cudaDeviceGetAttribute(&maxShared, cudaDevAttrMaxSharedMemoryPerBlockOptin, device), "cudaDeviceGetAttribute");
+  require(b->smemPerBlock <= maxShared, "Device shared memory is too small for this model");
+  b->hostModel = hm;
+  b->modelBytes = sizeof(DevModel<R>);
+  check(cudaMalloc(&b->devModel, sizeof(DevModel<R>)), "cudaMalloc model");
+  size_t pointBytes = std::max<size_t>(1, hm->points.size()) * sizeof(R);
+  check(cudaMalloc(&b->points, pointBytes), "cudaMalloc points");
+  check(cudaMalloc(&b->records, size_t(n) * b->recordStride * sizeof(R)), "cudaMalloc records");
+  check(cudaMemsetAsync(b->records, 0, size_t(n) * b->recordStride * sizeof(R), s), "cudaMemsetAsync");
+  check(cudaMemcpyAsync(b->devModel, &hm->dev, sizeof(DevModel<R>), cudaMemcpyHostToDevice, s), "copy model");
+  if (!hm->points.empty())
+    check(cudaMemcpyAsync(b->points, hm->points.data(), hm->points.size() * sizeof(R), cudaMemcpyHostToDevice, s),
+          "copy points");
+  setupAdvance<R>(b.get());
+  launchReset<R>(b.get(), nullptr, nullptr, nullptr, 0, s);
+  check(cudaGetLastError(), "initialise");
+  check(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+  check(cudaEventCreateWithFlags(&b->ready, cudaEventDisableTiming), "cudaEventCreate");
+  check(cudaEventRecord(b->ready, s), "cudaEventRecord");
+  return b.release();
+}
+
+template <class F> int guarded(F &&f) {
+  try {
+    f();
+    return DUCK_OK;
+  } catch (const std::invalid_argument &e) {
+    lastError = e.what();
+    return DUCK_EINVAL;
+  } catch (const CudaError &e) {
+    lastError = e.what();
+    return DUCK_ECUDA;
+  } catch (const std::exception &e) {
+    lastError = e.what();
+    return DUCK_EMODEL;
+  }
+}
+
+}  // namespace
+
+namespace {
+template <class R> void snapshot(duck_batch *b, void *bodies, void *joints, void *diag, cudaStream_t s) {
+  long long items = (long long)b->n * (b->nb + b->nj + 1);
+  snapshotKernel<R><<<blocksFor(items, 256), 256, 0, s>>>(
+      static_cast<const DevModel<R> *>(b->devModel), static_cast<const R *>(b->records), b->recordStride, b->n,
+      static_cast<R *>(bodies), static_cast<R *>(joints), static_cast<R *>(diag));
+  ++b->launches;
+}
+template <class R> void forcesLaunch(duck_batch *b, void *out, int groundOnly, cudaStream_t s) {
+  contactForcesKernel<R><<<blocksFor(b->n, 128), 128, 0, s>>>(
+      static_cast<const DevModel<R> *>(b->devModel), static_cast<const R *>(b->records), b->recordStride, b->n,
+      static_cast<R *>(out), groundOnly);
+  ++b->launches;
+}
+template <class R> void statsLaunch(duck_batch *b, void *counts, void *self, cudaStream_t s) {
+  contactStatsKernel<R><<<blocksFor(b->n, 128), 128, 0, s>>>(
+      static_cast<const DevModel<R> *>(b->devModel), static_cast<const R *>(b->records), b->recordStride, b->n,
+      static_cast<R *>(counts), static_cast<R *>(self));
+  ++b->launches;
+}
+template <class R> void loadsLaunch(duck_batch *b, const void *offset, void *out, cudaStream_t s) {
+  generalizedLoadsKernel<R><<<blocksFor(b->n, 64), 64, 0, s>>>(
+      static_cast<const DevModel<R> *>(b->devModel), static_cast<const R *>(b->records), b->recordStride, b->n,
+      static_cast<const R *>(offset), static_cast<R *>(out));
+  ++b->launches;
+}
+}  // namespace
+
+extern "C" {
+
+const char *duck_last_error(void) { return lastError.c_str(); }
+
+int duck_batch_create(const char *model_path, int num_envs, double dt, int iterations, int device, int fp64,
+                      int specialized, int shared_memory, duck_stream stream, duck_batch **out) {
+  return guarded([&] {
+    require(out != nullptr && model_path != nullptr, "Invalid arguments");
+    *out = nullptr;
+    require(specialized || !shared_memory, "Shared memory requires the compact MicroDuck backend");
+    require(num_envs > 0 && num_envs <= 65536 && dt > 0 && std::isfinite(dt) && iterations > 0,
+            "Invalid batch parameters");
+    DeviceGuard guard(device);
+    ParsedModel parsed = parseDuck(model_path);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    *out = fp64 ? create<double>(parsed, num_envs, dt, iterations, device, specialized, s)
+                : create<float>(parsed, num_envs, dt, iterations, device, specialized, s);
+  });
+}
+
+void duck_batch_destroy(duck_batch *b) {
+  if (!b) return;
+  cudaSetDevice(b->device);
+  if (b->ready) {
+    cudaEventSynchronize(b->ready);
+    cudaEventDestroy(b->ready);
+  }
+  cudaFree(b->devModel);
+  cudaFree(b->points);
+  cudaFree(b->records);
+  delete b;
+}
+
+int duck_batch_info(const duck_batch *b, int32_t *out) {
+  return guarded([&] {
+    require(b && out, "Invalid arguments");
+    int32_t v[10] = {b->n, b->nb, b->nj, b->bound, b->recordLength, b->fp64, b->device, b->teamsPerBlock, b->T,
+                     b->smemPerBlock};
+    std::memcpy(out, v, sizeof(v));
+  });
+}
+
+const char *duck_batch_joint_name(const duck_batch *b, int index) {
+  if (!b || index < 0 || index >= int(b->names.size())) return nullptr;
+  return b->names[index].c_str();
+}
+
+int duck_batch_reset(duck_batch *b, const uint8_t *mask, const void *q, const void *roots, duck_stream stream) {
+  return guarded([&] {
+    require(b && mask && roots && (q || b->nj == 0), "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    begin(b, s);
+    if (b->fp64) launchReset<double>(b, mask, q, roots, 1, s);
+    else launchReset<float>(b, mask, q, roots, 1, s);
+    finish(b, s);
+  });
+}
+
+int duck_batch_step(duck_batch *b, const void *target, const void *forces, int substeps, double kp, double limit,
+                    duck_stream stream) {
+  return guarded([&] {
+    require(b && forces && (target || b->nj == 0), "Invalid arguments");
+    // Zero selects the uncapped PD spring (extension.cu:290-294).
+    require(substeps > 0 && kp >= 0 && std::isfinite(kp) && limit >= 0 && std::isfinite(limit), "Invalid controls");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    StepArgs args{target, forces, nullptr, substeps, kp, limit};
+    begin(b, s);
+    if (b->fp64) launchAdvance<double>(b, args, s);
+    else launchAdvance<float>(b, args, s);
+    finish(b, s);
+  });
+}
+
+int duck_batch_step_motor(duck_batch *b, const void *motor, const void *forces, duck_stream stream) {
+  return guarded([&] {
+    require(b && forces && (motor || b->nj == 0), "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    StepArgs args{nullptr, forces, motor, 1, 0.0, 0.0};
+    begin(b, s);
+    if (b->fp64) launchAdvance<double>(b, args, s);
+    else launchAdvance<float>(b, args, s);
+    finish(b, s);
+  });
+}
+
+
+int duck_batch_state(duck_batch *b, void *bodies, void *joints, void *diag, duck_stream stream) {
+  return guarded([&] {
+    require(b && bodies && joints && diag, "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    begin(b, s);
+    if (b->fp64) snapshot<double>(b, bodies, joints, diag, s);
+    else snapshot<float>(b, bodies, joints, diag, s);
+    finish(b, s);
+  });
+}
+
+int duck_batch_contact_forces(duck_batch *b, void *out, int ground_only, duck_stream stream) {
+  return guarded([&] {
+    require(b && out, "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    begin(b, s);
+    if (b->fp64) forcesLaunch<double>(b, out, ground_only, s);
+    else forcesLaunch<float>(b, out, ground_only, s);
+    finish(b, s);
+  });
+}
+
+int duck_batch_self_contact_stats(duck_batch *b, void *out, duck_stream stream) {
+  return guarded([&] {
+    require(b && out, "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    begin(b, s);
+    if (b->fp64) statsLaunch<double>(b, nullptr, out, s);
+    else statsLaunch<float>(b, nullptr, out, s);
+    finish(b, s);
+  });
+}
+
+int duck_batch_contact_counts(duck_batch *b, void *out, duck_stream stream) {
+  return guarded([&] {
+    require(b && out, "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    begin(b, s);
+    if (b->fp64) statsLaunch<double>(b, out, nullptr, s);
+    else statsLaunch<float>(b, out, nullptr, s);
+    finish(b, s);
+  });
+}
+
+int duck_batch_generalized_loads(duck_batch *b, const void *offset, void *out, duck_stream stream) {
+  return guarded([&] {
+    require(b && offset && out, "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    begin(b, s);
+    if (b->fp64) loadsLaunch<double>(b, offset, out, s);
+    else loadsLaunch<float>(b, offset, out, s);
+    finish(b, s);
+  });
+}
+
+int duck_batch_export(duck_batch *b, int first, int count, void *records, duck_stream stream) {
+  return guarded([&] {
+    require(b && records && first >= 0 && count >= 0 && first + count <= b->n, "Invalid environment range");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const size_t real = b->fp64 ? 8 : 4;
+    begin(b, s);
+    if (count > 0)
+      check(cudaMemcpy2DAsync(records, b->recordLength * real,
+                              static_cast<char *>(b->records) + size_t(first) * b->recordStride * real,
+                              b->recordStride * real, b->recordLength * real, count, cudaMemcpyDeviceToDevice, s),
+            "export copy");
+    finish(b, s);
+  });
+}
+
+int duck_batch_import(duck_batch *b, int first, int count, const void *records, duck_stream stream) {
+  return guarded([&] {
+    require(b && records && first >= 0 && count >= 0 && first + count <= b->n, "Invalid environment range");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const size_t real = b->fp64 ? 8 : 4;
+    begin(b, s);
+    if (count > 0)
+      check(cudaMemcpy2DAsync(static_cast<char *>(b->records) + size_t(first) * b->recordStride * real,
+                              b->recordStride * real, records, b->recordLength * real, b->recordLength * real, count,
+                              cudaMemcpyDeviceToDevice, s),
+            "import copy");
+    finish(b, s);
+  });
+}
+
+int duck_batch_contact_keys(duck_batch *b, int env, int32_t *keys, int capacity, int *count, duck_stream stream) {
+  return guarded([&] {
+    require(b && keys && count && env >= 0 && env < b->n && capacity >= 0, "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const size_t real = b->fp64 ? 8 : 4;
+    std::vector<char> rec(b->recordLength * real);
+    begin(b, s);
+    check(cudaMemcpyAsync(rec.data(), static_cast<char *>(b->records) + size_t(env) * b->recordStride * real,
+                          rec.size(), cudaMemcpyDeviceToHost, s),
+          "contact copy");
+    finish(b, s);
+    check(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    auto value = [&](int i) {
+      return b->fp64 ? reinterpret_cast<double *>(rec.data())[i] : double(reinterpret_cast<float *>(rec.data())[i]);
+    };
+    const int n = int(value(1));
+    const int base = kRecHeader + kRecBody * b->nb + kRecJoint * b->nj;
+    for (int i = 0; i < std::min(n, capacity); ++i)
+      for (int k = 0; k < 5; ++k) keys[5 * i + k] = int32_t(value(base + kRecContact * i + (k == 4 ? 4 : k)));
+    *count = n;
+  });
+}
+
+int duck_batch_reference(duck_batch *b, const void *target, const void *forces, int substeps, double kp,
+                         double limit, void *bodies, void *joints, void *diag) {
+  return guarded([&] {
+    require(b && forces && bodies && diag && (target || b->nj == 0) && (joints || b->nj == 0) && substeps > 0, "Invalid CPU reference inputs");
+    DeviceGuard guard(b->device);
+    const size_t real = b->fp64 ? 8 : 4;
+    // A private one-environment batch sharing this batch's device model.
+    duck_batch one = *b;
+    one.n = 1;
+    one.ready = nullptr;
+    void *scratch = nullptr;
+    const size_t bytes = size_t(one.recordStride) * real;
+    size_t ioBytes = (b->nj + 3 + 13 * b->nb + 2 * b->nj + 6) * real;
+    check(cudaMalloc(&scratch, bytes + ioBytes), "cudaMalloc reference");
+    std::unique_ptr<void, void (*)(void *)> hold(scratch, [](void *p) { cudaFree(p); });
+    one.records = scratch;
+    char *io = static_cast<char *>(scratch) + bytes;
+    char *dTarget = io, *dForces = io + b->nj * real, *dBodies = dForces + 3 * real,
+         *dJoints = dBodies + 13 * b->nb * real, *dDiag = dJoints + 2 * b->nj * real;
+    cudaStream_t s = nullptr;
+    check(cudaMemcpy(dTarget, target, b->nj * real, cudaMemcpyHostToDevice), "copy target");
+    check(cudaMemcpy(dForces, forces, 3 * real, cudaMemcpyHostToDevice), "copy forces");
+    if (b->fp64) launchReset<double>(&one, nullptr, nullptr, nullptr, 0, s);
+    else launchReset<float>(&one, nullptr, nullptr, nullptr, 0, s);
+    StepArgs args{dTarget, dForces, nullptr, substeps, kp, limit};
+    if (b->fp64) { launchAdvance<double>(&one, args, s); snapshot<double>(&one, dBodies, dJoints, dDiag, s); }
+    else { launchAdvance<float>(&one, args, s); snapshot<float>(&one, dBodies, dJoints, dDiag, s); }
+    check(cudaGetLastError(), "reference launch");
+    check(cudaMemcpy(bodies, dBodies, 13 * b->nb * real, cudaMemcpyDeviceToHost), "copy bodies");
+    check(cudaMemcpy(joints, dJoints, 2 * b->nj * real, cudaMemcpyDeviceToHost), "copy joints");
+    check(cudaMemcpy(diag, dDiag, 6 * real, cudaMemcpyDeviceToHost), "copy diag");
+    b->launches += one.launches - b->launches;
+  });
+}
+
+int64_t duck_batch_launches(const duck_batch *b) { return b ? b->launches : 0; }
+
+int duck_fp32_peak(int device, int iterations, double *tflops, duck_stream stream) {
+  return guarded([&] {
+    require(tflops && iterations > 0, "Invalid arguments");
+    DeviceGuard guard(device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int sms = 0;
+    check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "cudaDeviceGetAttribute");
+    float *sink = nullptr;
+    check(cudaMalloc(&sink, sizeof(float)), "cudaMalloc sink");
+    std::unique_ptr<float, void (*)(float *)> hold(sink, [](float *p) { cudaFree(p); });
+    cudaEvent_t start, stop;
+    check(cudaEventCreate(&start), "cudaEventCreate");
+    check(cudaEventCreate(&stop), "cudaEventCreate");
+    const int blocks = sms * 8, threads = 256;
+    fmaPeakKernel<<<blocks, threads, 0, s>>>(sink, iterations / 10 + 1, 1.0f);
+    check(cudaEventRecord(start, s), "cudaEventRecord");
+    fmaPeakKernel<<<blocks, threads, 0, s>>>(sink, iterations, 1.0f);
+    check(cudaEventRecord(stop, s), "cudaEventRecord");
+    check(cudaEventSynchronize(stop), "cudaEventSynchronize");
+    float ms = 0;
+    check(cudaEventElapsedTime(&ms, start, stop), "cudaEventElapsedTime");
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+    *tflops = 2.0 * 8.0 * double(iterations) * blocks * threads / (ms * 1e-3) / 1e12;
+  });
+}
+
+}  // extern "C"

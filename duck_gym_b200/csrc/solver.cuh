@@ -1,0 +1,1005 @@
+// The AVBD environment step on sm_100a: one team of T lanes per environment
+// (T = 8 for the biped, four environments per warp), every environment's
+// working state kept in shared memory for all substeps of a call.
+//
+// Algorithm: the reference's BasicState::advance / step (src/cuda/kernel.cuh:
+// 421-443, 937-1095) -- contact generation, joint warm start and predictor,
+// colored Gauss-Seidel block solves, augmented-Lagrangian dual and penalty
+// updates with the friction-cone clamp, velocity recovery and diagnostics.
+// What differs is the mapping onto the GPU:
+//  * the reference runs one 32-lane warp per environment and executes the
+//    warm start, predictor, contact construction and velocity recovery on
+//    lane 0; here every phase is spread over the team (a lane per body, joint,
+//    shape or contact), and 4 environments share a warp;
+//  * the primal update of a body exploits the structure of each Jacobian row
+//    (unit-axis linear rows, pure angular rows) and assembles only the lower
+//    triangle of the 6x6 block; all hinge-axis terms (limits, PD drive,
+//    damping, dry friction) are summed into one rank-one update;
+//  * the frozen world inertia of a body is formed once per substep;
+//  * contact generation reproduces the reference's arithmetic bit for bit
+//    (x-prefixed ops of dmath.cuh) so contact sets match the CPU exactly.
+#pragma once
+#include "dmath.cuh"
+#include "model.hpp"
+
+namespace duckb200 {
+
+// Portable record: header 8, bodies B x 16, joints J x 22, contacts bound x 32.
+constexpr int kRecHeader = 8, kRecBody = 16, kRecJoint = 22, kRecContact = 32;
+// On-chip contact entry: meta, keys, feature, local(3), anchor/localB(3),
+// friction, c0, lambda(3), penalty(3).
+constexpr int kC = 17;
+enum { cMeta = 0, cKey = 1, cFeature = 2, cLocal = 3, cAnchor = 6, cFriction = 9, cC0 = 10,
+       cLambda = 11, cPenalty = 14 };
+// Team-shared integers.
+enum { iFailed = 0, iCount = 1, iGround = 2, iColors = 3, iPrevCount = 4, iMisc = 8 };
+
+struct Layout {
+  int X, Q, XP, QP, X0, Q0, V, W, IW, F1, KP;          // bodies, base force, kp/limit
+  int JL, JP, JC0, JA0, JV0, JLF, JPF, JT, JTQ, JFL, JD;  // joints
+  int C, CB;                                           // contacts, self-contact basis
+  int I;                                               // ints (Real slot offset)
+  int colors, colorList, colorStart;                   // offsets inside the int region
+  int cap, pairCap, maxColors;
+  int size;                                            // Reals per environment
+};
+
+template <class R> __host__ inline Layout makeLayout(const DevModel<R> &m) {
+  Layout L{};
+  int o = 0;
+  auto take = [&](int n) { int at = o; o += n; return at; };
+  const int nb = m.nb, nj = m.nj;
+  L.X = take(3 * nb); L.Q = take(4 * nb); L.XP = take(3 * nb); L.QP = take(4 * nb);
+  L.X0 = take(3 * nb); L.Q0 = take(4 * nb); L.V = take(3 * nb); L.W = take(3 * nb);
+  L.IW = take(6 * nb); L.F1 = take(3); L.KP = take(2);
+  L.JL = take(7 * nj); L.JP = take(7 * nj); L.JC0 = take(7 * nj); L.JA0 = take(nj);
+  L.JV0 = take(nj); L.JLF = take(nj); L.JPF = take(nj); L.JT = take(nj); L.JTQ = take(nj);
+  L.JFL = take(nj); L.JD = take(nj);
+  L.cap = m.groundCap + m.np;
+  L.pairCap = m.np;
+  L.C = take(kC * std::max(L.cap, 1));
+  L.CB = take(9 * std::max(L.pairCap, 1));
+  L.maxColors = 2 + m.np;
+  int ints = iMisc + nb + nb + L.maxColors + 1;
+  L.colors = iMisc;
+  L.colorList = iMisc + nb;
+  L.colorStart = iMisc + 2 * nb;
+  L.I = take(int((ints * sizeof(int) + sizeof(R) - 1) / sizeof(R)));
+  // Pad so consecutive environments start on different banks.
+  int padded = (o + 3) & ~3;
+  if ((padded % 32) == 0) padded += 4;
+  L.size = padded;
+  return L;
+}
+
+template <class T> __device__ __forceinline__ T ldg(const T &v) { return __ldg(&v); }
+
+template <int T> struct Team {
+  unsigned mask;
+  int lane;
+  __device__ __forceinline__ Team() {
+    int l = threadIdx.x & 31;
+    lane = l & (T - 1);
+    mask = T == 32 ? 0xffffffffu : (((1u << T) - 1u) << (l & ~(T - 1)));
+  }
+  __device__ __forceinline__ void sync() const { __syncwarp(mask); }
+  template <class V> __device__ __forceinline__ V max(V v) const {
+#pragma unroll
+    for (int o = T / 2; o > 0; o >>= 1) {
+      V u = __shfl_xor_sync(mask, v, o, T);
+      v = v > u ? v : u;
+    }
+    return v;
+  }
+  __device__ __forceinline__ bool any(bool p) const { return __any_sync(mask, p); }
+  // Exclusive prefix sum over the team; *total receives the team sum.
+  __device__ __forceinline__ int scan(int v, int *total) const {
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < T; o <<= 1) {
+      int y = __shfl_up_sync(mask, x, o, T);
+      if (lane >= o) x += y;
+    }
+    *total = __shfl_sync(mask, x, T - 1, T);
+    return x - v;
+  }
+};
+
+struct StepArgs {
+  const void *target;   // [E,J] (step) or nullptr
+  const void *forces;   // [E,3]
+  const void *motor;    // [E,J,3] (step_motor) or nullptr
+  int substeps;
+  double kp, limit;
+};
+
+template <class R, int T> struct Solver {
+  const DevModel<R> *__restrict__ m;
+  const R *__restrict__ pts;
+  R *S;        // environment's shared-memory block
+  int *I;      // its integer region
+  R *rec;      // environment's global record
+  const Layout &L;
+  Team<T> team;
+
+  __device__ Solver(const DevModel<R> *model, const R *points, R *smem, R *record, const Layout &layout)
+      : m(model), pts(points), S(smem), rec(record), L(layout) {
+    I = reinterpret_cast<int *>(S + L.I);
+  }
+
+  // ------------------------------------------------------------ accessors
+  __device__ __forceinline__ V3<R> ld3(int off) const { return {S[off], S[off + 1], S[off + 2]}; }
+  __device__ __forceinline__ Q4<R> ld4(int off) const { return {S[off], S[off + 1], S[off + 2], S[off + 3]}; }
+  __device__ __forceinline__ void st3(int off, V3<R> v) { S[off] = v.x; S[off + 1] = v.y; S[off + 2] = v.z; }
+  __device__ __forceinline__ void st4(int off, Q4<R> q) { S[off] = q.w; S[off + 1] = q.x; S[off + 2] = q.y; S[off + 3] = q.z; }
+  __device__ __forceinline__ V3<R> mv3(const R (&a)[3]) const { return {ldg(a[0]), ldg(a[1]), ldg(a[2])}; }
+  __device__ __forceinline__ Q4<R> mq4(const R (&a)[4]) const { return {ldg(a[0]), ldg(a[1]), ldg(a[2]), ldg(a[3])}; }
+  __device__ __forceinline__ V3<R> bodyForce(int b) const {
+    return b == 1 ? ld3(L.F1) : V3<R>{R(0), R(0), R(0)};
+  }
+  __device__ __forceinline__ R *contact(int c) { return S + L.C + kC * c; }
+  __device__ __forceinline__ int &cmeta(int c) { return reinterpret_cast<int &>(S[L.C + kC * c + cMeta]); }
+  __device__ __forceinline__ int &ckey(int c) { return reinterpret_cast<int &>(S[L.C + kC * c + cKey]); }
+  __device__ __forceinline__ int &cfeat(int c) { return reinterpret_cast<int &>(S[L.C + kC * c + cFeature]); }
+  // meta: body | (other + 1) << 8 | stick << 16
+  __device__ static __forceinline__ int metaBody(int meta) { return meta & 0xff; }
+  __device__ static __forceinline__ int metaOther(int meta) { return ((meta >> 8) & 0xff) - 1; }
+  __device__ static __forceinline__ bool metaStick(int meta) { return (meta >> 16) & 1; }
+
+  // ------------------------------------------------------------ load / store
+  // Record -> shared memory.  Contacts stay in the record: the first
+  // substep's warm start reads them from there.
+  __device__ void load() {
+    const int nb = m->nb, nj = m->nj;
+    for (int b = team.lane; b < nb; b += T) {
+      const R *r = rec + kRecHeader + kRecBody * b;
+      st3(L.X + 3 * b, {r[0], r[1], r[2]});
+      st4(L.Q + 4 * b, {r[3], r[4], r[5], r[6]});
+      st3(L.V + 3 * b, {r[7], r[8], r[9]});
+      st3(L.W + 3 * b, {r[10], r[11], r[12]});
+    }
+    for (int j = team.lane; j < nj; j += T) {
+      const R *r = rec + kRecHeader + kRecBody * nb + kRecJoint * j;
+#pragma unroll
+      for (int k = 0; k < 7; ++k) {
+        S[L.JL + 7 * j + k] = r[k];
+        S[L.JP + 7 * j + k] = r[7 + k];
+      }
+      S[L.JLF + j] = r[14];
+      S[L.JPF + j] = r[15];
+      S[L.JT + j] = r[16];
+      S[L.JTQ + j] = r[19];
+      S[L.JFL + j] = r[20];
+      S[L.JD + j] = r[21];
+    }
+    if (team.lane == 0) {
+      const R *r = rec + kRecHeader + kRecBody * 1;
+      st3(L.F1, {r[13], r[14], r[15]});
+      I[iFailed] = int(rec[0]);
+      I[iPrevCount] = int(rec[1]);
+      I[iCount] = 0;
+    }
+  }
+  // Shared memory -> record (bodies, joints, header); contacts are written at
+  // the end of every substep.
+  __device__ void store(R kp, R limit) {
+    const int nb = m->nb, nj = m->nj;
+    for (int b = team.lane; b < nb; b += T) {
+      R *r = rec + kRecHeader + kRecBody * b;
+      V3<R> x = ld3(L.X + 3 * b), v = ld3(L.V + 3 * b), w = ld3(L.W + 3 * b);
+      Q4<R> q = ld4(L.Q + 4 * b);
+      r[0] = x.x; r[1] = x.y; r[2] = x.z; r[3] = q.w; r[4] = q.x; r[5] = q.y; r[6] = q.z;
+      r[7] = v.x; r[8] = v.y; r[9] = v.z; r[10] = w.x; r[11] = w.y; r[12] = w.z;
+      if (b == 1) { V3<R> f = ld3(L.F1); r[13] = f.x; r[14] = f.y; r[15] = f.z; }
+    }
+    for (int j = team.lane; j < nj; j += T) {
+      R *r = rec + kRecHeader + kRecBody * nb + kRecJoint * j;
+#pragma unroll
+      for (int k = 0; k < 7; ++k) {
+        r[k] = S[L.JL + 7 * j + k];
+        r[7 + k] = S[L.JP + 7 * j + k];
+      }
+      r[14] = S[L.JLF + j]; r[15] = S[L.JPF + j]; r[16] = S[L.JT + j]; r[17] = kp;
+      r[18] = limit; r[19] = S[L.JTQ + j]; r[20] = S[L.JFL + j]; r[21] = S[L.JD + j];
+    }
+  }
+  __device__ void storeHeader(R jointError, R penetration, int contacts, bool converged, R axisError,
+                              int iterations) {
+    if (team.lane == 0) {
+      rec[0] = R(I[iFailed]);
+      rec[2] = jointError; rec[3] = penetration; rec[4] = R(contacts); rec[5] = R(converged);
+      rec[6] = axisError; rec[7] = R(iterations);
+    }
+  }
+  // On-chip contact list -> record (the warm-start cache of the next substep).
+  __device__ void storeContacts() {
+    const int n = I[iCount], nGround = I[iGround];
+    R *base = rec + kRecHeader + kRecBody * m->nb + kRecJoint * m->nj;
+    for (int c = team.lane; c < n; c += T) {
+      const R *s = contact(c);
+      R *r = base + kRecContact * c;
+      int meta = cmeta(c), key = ckey(c);
+      int other = metaOther(meta);
+      r[0] = R(metaBody(meta)); r[1] = R(key & 0xffff); r[2] = R(cfeat(c)); r[3] = R(other);
+      r[4] = R((key >> 16) - 1); r[5] = R(metaStick(meta) ? 1 : 0);
+      r[6] = s[cLocal]; r[7] = s[cLocal + 1]; r[8] = s[cLocal + 2];
+      if (other < 0) {
+        r[9] = s[cAnchor]; r[10] = s[cAnchor + 1]; r[11] = s[cAnchor + 2];
+        r[12] = r[13] = r[14] = R(0);
+        r[15] = R(1); r[16] = R(0); r[17] = R(0); r[18] = R(0); r[19] = R(1); r[20] = R(0);
+        r[21] = R(0); r[22] = R(0); r[23] = R(1);
+      } else {
+        const R *bs = S + L.CB + 9 * (c - nGround);
+        r[9] = r[10] = r[11] = R(0);
+        r[12] = s[cAnchor]; r[13] = s[cAnchor + 1]; r[14] = s[cAnchor + 2];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) r[15 + k] = bs[k];
+      }
+      r[24] = s[cFriction]; r[25] = s[cC0];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) { r[26 + k] = s[cLambda + k]; r[29 + k] = s[cPenalty + k]; }
+    }
+    if (team.lane == 0) rec[1] = R(n);
+  }
+
+  // ------------------------------------------------------------ contacts
+  // Support point k of a ground shape in body coordinates (kernel.cuh:576-583).
+  __device__ V3<R> xpoint(int s, Q4<R> q, int k) const {
+    int type = ldg(m->sType[s]);
+    if (type == 1 || type == 3) {
+      const R *p = pts + 3 * (ldg(m->sOffset[s]) + k);
+      return {ldg(p[0]), ldg(p[1]), ldg(p[2])};
+    }
+    V3<R> size = mv3(m->sSize[s]), center = mv3(m->sCenter[s]);
+    V3<R> down = xrotate(conj(q), V3<R>{R(0), R(0), -size.x});
+    if (type == 0) return xadd(center, down);
+    V3<R> off = xrotate(mq4(m->sQ[s]), V3<R>{R(0), R(0), xmul(R(k ? 1 : -1), size.y)});
+    return xadd(xadd(center, off), down);
+  }
+  // Up to four lowest, laterally separated support points of shape s that are
+  // predicted below 3 mm (kernel.cuh:338-364, 601-653), on one lane.
+  __device__ int groundPicks(int s, int *feature, V3<R> *world) const {
+    const int b = ldg(m->sBody[s]);
+    const R mass = ldg(m->mass[b]);
+    if (!m->ground || !ldg(m->sGround[s]) || mass == R(0)) return 0;
+    const R dt = m->dt;
+    V3<R> x = ld3(L.X + 3 * b), v = ld3(L.V + 3 * b), w = ld3(L.W + 3 * b);
+    Q4<R> q = ld4(L.Q + 4 * b);
+    const R accel = xadd(m->gravity[2], bodyForce(b).z / mass);
+    const R dt2 = xmul(dt, dt);
+    R low = rmin(x.z, xadd(xadd(x.z, xmul(dt, v.z)), xmul(dt2, accel)));
+    if (double(xsub(low, xmul(ldg(m->sRadius[s]), xadd(R(1), xmul(dt, xnorm(w)))))) >= .003) return 0;
+    const int count = ldg(m->sCount[s]);
+    int n = 0;
+    for (int pick = 0; pick < 4; ++pick) {
+      int best = -1;
+      R lowest = R(INFINITY);
+      V3<R> bestWorld{};
+      for (int k = 0; k < count; ++k) {
+        V3<R> local = xpoint(s, q, k), wp = xadd(x, xrotate(q, local));
+        V3<R> vel = xadd(v, xcross(w, xsub(wp, x)));
+        R z = rmin(wp.z, xadd(xadd(wp.z, xmul(dt, vel.z)), xmul(dt2, accel)));
+        if (double(z) >= .003 || z >= lowest) continue;
+        bool duplicate = false;
+        for (int c = 0; c < n; ++c)
+          if (double(xhypot(xsub(world[c].x, wp.x), xsub(world[c].y, wp.y))) < .005) duplicate = true;
+        if (duplicate) continue;
+        best = k;
+        lowest = z;
+        bestWorld = wp;
+      }
+      if (best < 0) break;
+      feature[n] = best;
+      world[n] = bestWorld;
+      ++n;
+    }
+    return n;
+  }
+  // Ground contact with warm start from the record (kernel.cuh:618-650).
+  __device__ void buildGround(int slot, int s, int best, V3<R> bestWorld, int prevCount) {
+    const int b = ldg(m->sBody[s]);
+    V3<R> x = ld3(L.X + 3 * b);
+    Q4<R> q = ld4(L.Q + 4 * b);
+    V3<R> local = xpoint(s, q, best);
+    V3<R> anchor{bestWorld.x, bestWorld.y, R(0)};
+    R lambda[3] = {R(0), R(0), R(0)}, penalty[3] = {R(1000), R(1000), R(1000)};
+    const R *prev = rec + kRecHeader + kRecBody * m->nb + kRecJoint * m->nj;
+    for (int i = 0; i < prevCount; ++i) {
+      const R *p = prev + kRecContact * i;
+      if (p[3] < R(0) && int(p[1]) == s && int(p[2]) == best) {
+#pragma unroll
+        for (int d = 0; d < 3; ++d) { lambda[d] = p[26 + d]; penalty[d] = p[29 + d]; }
+        if (p[5] != R(0)) {
+          local = {p[6], p[7], p[8]};
+          anchor = {p[9], p[10], p[11]};
+        }
+        break;
+      }
+    }
+    const R c0 = rmin(xadd(x, xrotate(q, local)).z, R(0));
+    const R ag = xmul(m->alpha, m->gamma);
+    R *c = contact(slot);
+    cmeta(slot) = b | (0 << 8);
+    ckey(slot) = s | (0 << 16);
+    cfeat(slot) = best;
+    c[cLocal] = local.x; c[cLocal + 1] = local.y; c[cLocal + 2] = local.z;
+    c[cAnchor] = anchor.x; c[cAnchor + 1] = anchor.y; c[cAnchor + 2] = anchor.z;
+    c[cFriction] = ldg(m->sFriction[s]);
+    c[cC0] = c0;
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      c[cLambda + d] = xmul(lambda[d], ag);
+      c[cPenalty + d] = rclamp(xmul(penalty[d], m->gamma), R(1000), R(1e9));
+    }
+  }
+
+#include "mpr.cuh"
+
+  __device__ void detectContacts() {
+    const int nb = m->nb;
+    for (int b = team.lane; b < nb; b += T) I[L.colors + b] = ldg(m->color[b]);
+    if (team.lane == 0) I[iColors] = 2;
+    const int prevCount = I[iPrevCount];
+    int base = 0;
+    for (int first = 0; first < m->ns; first += T) {
+      const int s = first + team.lane;
+      int feature[4];
+      V3<R> world[4];
+      int n = s < m->ns ? groundPicks(s, feature, world) : 0;
+      int total;
+      int offset = team.scan(n, &total);
+      for (int k = 0; k < n; ++k) {
+        int slot = base + offset + k;
+        if (slot < L.cap) buildGround(slot, s, feature[k], world[k], prevCount);
+        else I[iFailed] = 1;
+      }
+      base += total;
+    }
+    base = base < L.cap ? base : L.cap;
+    team.sync();
+    if (team.lane == 0) I[iGround] = base;
+    if (m->np > 0) base = detectPairs(base, prevCount);
+    if (team.lane == 0) I[iCount] = base;
+    team.sync();
+  }
+
+  // Colour lists of the dynamic bodies; contacts between equal colours move
+  // the second body to a fresh colour (kernel.cuh:717-720).
+  __device__ void buildColorLists() {
+    if (team.lane == 0) {
+      const int nb = m->nb, colorCount = I[iColors];
+      int fill = 0;
+      for (int c = 0; c < colorCount; ++c) {
+        I[L.colorStart + c] = fill;
+        for (int b = 0; b < nb; ++b)
+          if (I[L.colors + b] == c && ldg(m->mass[b]) > R(0)) I[L.colorList + fill++] = b;
+      }
+      I[L.colorStart + colorCount] = fill;
+    }
+    team.sync();
+  }
+
+  // ------------------------------------------------------------ joints
+  struct JointGeo {
+    V3<R> ra, rb, axis, axisB, t1, t2;
+    R C[7];
+    R angle;
+  };
+  __device__ __forceinline__ void evalJoint(int j, JointGeo &e) const {
+    const int a = ldg(m->ja[j]), b = ldg(m->jb[j]);
+    Q4<R> qa = ld4(L.Q + 4 * a), qb = ld4(L.Q + 4 * b);
+    V3<R> xa = ld3(L.X + 3 * a), xb = ld3(L.X + 3 * b);
+    e.ra = rotate(qa, mv3(m->ra[j]));
+    e.rb = rotate(qb, mv3(m->rb[j]));
+    V3<R> d = xa + e.ra - xb - e.rb;
+    e.C[0] = d.x; e.C[1] = d.y; e.C[2] = d.z;
+    e.axis = rotate(qa, mv3(m->axisA[j]));
+    e.axisB = rotate(qb, mv3(m->axisB[j]));
+    e.t1 = rotate(qa, mv3(m->tangentA[j]));
+    e.t2 = cross(e.axis, e.t1);
+    e.C[3] = dot(e.t1, e.axisB);
+    e.C[4] = dot(e.t2, e.axisB);
+    V3<R> u = rotate(qb, mv3(m->tangentB[j]));
+    e.angle = atan2(dot(e.axis, cross(e.t1, u)), dot(e.t1, u));
+    e.C[5] = e.angle - ldg(m->lo[j]);
+    e.C[6] = ldg(m->hi[j]) - e.angle;
+  }
+
+  // ------------------------------------------------------------ 6x6 algebra
+  // Packed lower triangle: (i, j), j <= i, at i (i + 1) / 2 + j.
+  static __device__ __forceinline__ int tri(int i, int j) { return i * (i + 1) / 2 + j; }
+  // Row J = (e_k, r x e_k) with force f and stiffness p (kernel.cuh:164-176).
+  static __device__ __forceinline__ void stampLinear(R *H, R *g, int k, V3<R> r, R f, R p) {
+    V3<R> c = k == 0 ? V3<R>{R(0), r.z, -r.y} : (k == 1 ? V3<R>{-r.z, R(0), r.x} : V3<R>{r.y, -r.x, R(0)});
+    g[k] += f;
+    g[3] += c.x * f; g[4] += c.y * f; g[5] += c.z * f;
+    H[tri(k, k)] += p;
+    H[tri(3, k)] += p * c.x; H[tri(4, k)] += p * c.y; H[tri(5, k)] += p * c.z;
+    V3<R> pc = c * p;
+    H[tri(3, 3)] += pc.x * c.x;
+    H[tri(4, 3)] += pc.y * c.x; H[tri(4, 4)] += pc.y * c.y;
+    H[tri(5, 3)] += pc.z * c.x; H[tri(5, 4)] += pc.z * c.y; H[tri(5, 5)] += pc.z * c.z;
+  }
+  // Row J = (0, c).
+  static __device__ __forceinline__ void stampAngular(R *H, R *g, V3<R> c, R f, R p) {
+    g[3] += c.x * f; g[4] += c.y * f; g[5] += c.z * f;
+    V3<R> pc = c * p;
+    H[tri(3, 3)] += pc.x * c.x;
+    H[tri(4, 3)] += pc.y * c.x; H[tri(4, 4)] += pc.y * c.y;
+    H[tri(5, 3)] += pc.z * c.x; H[tri(5, 4)] += pc.z * c.y; H[tri(5, 5)] += pc.z * c.z;
+  }
+  // Dense row J = (e, c).
+  static __device__ __forceinline__ void stampDense(R *H, R *g, V3<R> e, V3<R> c, R f, R p) {
+    R J[6] = {e.x, e.y, e.z, c.x, c.y, c.z};
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      g[i] += J[i] * f;
+      R pj = p * J[i];
+#pragma unroll
+      for (int k = 0; k <= i; ++k) H[tri(i, k)] += pj * J[k];
+    }
+  }
+  // Diagonal majorizer of the rotational geometric stiffness (kernel.cuh:283-301).
+  static __device__ __forceinline__ void geometric(R *H, V3<R> r, V3<R> f) {
+    R rf = dot(r, f);
+    R a00 = r.x * f.x - rf, a11 = r.y * f.y - rf, a22 = r.z * f.z - rf;
+    R a01 = R(0.5) * (r.x * f.y + f.x * r.y);
+    R a02 = R(0.5) * (r.x * f.z + f.x * r.z);
+    R a12 = R(0.5) * (r.y * f.z + f.y * r.z);
+    H[tri(3, 3)] += fsqrt(a00 * a00 + a01 * a01 + a02 * a02);
+    H[tri(4, 4)] += fsqrt(a01 * a01 + a11 * a11 + a12 * a12);
+    H[tri(5, 5)] += fsqrt(a02 * a02 + a12 * a12 + a22 * a22);
+  }
+  // Friction-cone clamped contact force (kernel.cuh:304-315).
+  static __device__ __forceinline__ V3<R> coneForce(V3<R> C, const R *c) {
+    V3<R> f{c[cLambda] + c[cPenalty] * C.x, c[cLambda + 1] + c[cPenalty + 1] * C.y,
+            c[cLambda + 2] + c[cPenalty + 2] * C.z};
+    f.z = rmin(f.z, R(0));
+    R t = sqrt(f.x * f.x + f.y * f.y), bound = -c[cFriction] * f.z;
+    if (t > bound && t > R(0)) {
+      R s = bound / t;
+      f.x *= s;
+      f.y *= s;
+    }
+    return f;
+  }
+  // SO(3) log-Jacobian coefficient (1 - (a/2) cot(a/2)) / a^2, from its
+  // Bernoulli series below 0.5 rad (relative error < 1e-12 there) and from the
+  // closed form above, where it has no cancellation.
+  static __device__ __forceinline__ R logJacobianCoef(R a) {
+    if (a < R(0.5)) {
+      R a2 = a * a;
+      return R(1.0 / 12) + a2 * (R(1.0 / 720) + a2 * (R(1.0 / 30240) + a2 * (R(1.0 / 1209600) +
+                                                                               a2 * R(1.0 / 47900160))));
+    }
+    R h = R(0.5) * a;
+    R s, c;
+    sincosT(h, &s, &c);
+    return (R(1) - h * c / s) / (a * a);
+  }
+  // Solve H x = -g with a packed Cholesky factorisation (kernel.cuh:177-228);
+  // NaN on a non-positive pivot.
+  static __device__ __forceinline__ bool solve(const R *H, const R *g, R *x) {
+    R Lf[21], inv[6];
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+#pragma unroll
+      for (int j = 0; j <= i; ++j) {
+        R v = H[tri(i, j)];
+#pragma unroll
+        for (int k = 0; k < j; ++k) v -= Lf[tri(i, k)] * Lf[tri(j, k)];
+        if (i == j) {
+          if (!(v > R(0)) || !isfinite(v)) return false;
+          R l = sqrt(v);
+          Lf[tri(i, i)] = l;
+          inv[i] = R(1) / l;
+        } else {
+          Lf[tri(i, j)] = v * inv[j];
+        }
+      }
+    }
+    R y[6];
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      R v = -g[i];
+#pragma unroll
+      for (int k = 0; k < i; ++k) v -= Lf[tri(i, k)] * y[k];
+      y[i] = v * inv[i];
+    }
+#pragma unroll
+    for (int i = 5; i >= 0; --i) {
+      R v = y[i];
+#pragma unroll
+      for (int k = i + 1; k < 6; ++k) v -= Lf[tri(k, i)] * x[k];
+      x[i] = v * inv[i];
+    }
+    return true;
+  }
+
+  // ------------------------------------------------------------ primal
+  // Block update of body bi (kernel.cuh:828-936).
+  __device__ R updateBody(int bi, R kp, R limit) {
+    const R h = m->dt, alpha = m->alpha;
+    const R ih2 = R(1) / (h * h);
+    const R mass = ldg(m->mass[bi]);
+    R H[21], g[6];
+#pragma unroll
+    for (int i = 0; i < 21; ++i) H[i] = R(0);
+#pragma unroll
+    for (int i = 0; i < 6; ++i) g[i] = R(0);
+    V3<R> x = ld3(L.X + 3 * bi), xp = ld3(L.XP + 3 * bi);
+    Q4<R> q = ld4(L.Q + 4 * bi), qp = ld4(L.QP + 4 * bi);
+    // Inertia block with the SO(3) log Jacobian and frozen world inertia.
+    {
+      V3<R> dx = x - xp, th = qlog(qmul(q, conj(qp)));
+      R ml = mass * ih2;
+      H[tri(0, 0)] = ml; H[tri(1, 1)] = ml; H[tri(2, 2)] = ml;
+      g[0] = ml * dx.x; g[1] = ml * dx.y; g[2] = ml * dx.z;
+      R a2 = dot(th, th), a = sqrt(a2);
+      R coef = logJacobianCoef(a);
+      // rotJ[k] = e_k - theta x e_k / 2 + coef theta x (theta x e_k), as columns.
+      R J[3][3];
+      R d = R(1) - coef * a2;
+      R th3[3] = {th.x, th.y, th.z};
+#pragma unroll
+      for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int k = 0; k < 3; ++k) J[i][k] = coef * th3[i] * th3[k] + (i == k ? d : R(0));
+      // -(theta x e_k) / 2: theta x e_x = (0, tz, -ty), x e_y = (-tz, 0, tx),
+      // x e_z = (ty, -tx, 0).
+      J[1][0] -= R(0.5) * th.z; J[2][0] += R(0.5) * th.y;
+      J[0][1] += R(0.5) * th.z; J[2][1] -= R(0.5) * th.x;
+      J[0][2] -= R(0.5) * th.y; J[1][2] += R(0.5) * th.x;
+      const R *iw = S + L.IW + 6 * bi;   // xx, yy, zz, xy, xz, yz
+      R Iw[3][3] = {{iw[0], iw[3], iw[4]}, {iw[3], iw[1], iw[5]}, {iw[4], iw[5], iw[2]}};
+      R It[3], N[3][3];
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        It[i] = Iw[i][0] * th.x + Iw[i][1] * th.y + Iw[i][2] * th.z;
+#pragma unroll
+        for (int l = 0; l < 3; ++l) N[i][l] = Iw[i][0] * J[0][l] + Iw[i][1] * J[1][l] + Iw[i][2] * J[2][l];
+      }
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        g[3 + k] = (J[0][k] * It[0] + J[1][k] * It[1] + J[2][k] * It[2]) * ih2;
+#pragma unroll
+        for (int l = 0; l <= k; ++l)
+          H[tri(3 + k, 3 + l)] = (J[0][k] * N[0][l] + J[1][k] * N[1][l] + J[2][k] * N[2][l]) * ih2;
+      }
+    }
+    // Hinges touching bi, in CSR order.
+    const int adjEnd = ldg(m->csrOffset[bi + 1]);
+    for (int adj = ldg(m->csrOffset[bi]); adj < adjEnd; ++adj) {
+      const int j = ldg(m->csrJoint[adj]);
+      JointGeo e;
+      evalJoint(j, e);
+      const bool parent = ldg(m->ja[j]) == bi;
+      const R s = parent ? R(1) : R(-1);
+      const R *lam = S + L.JL + 7 * j, *pen = S + L.JP + 7 * j, *c0 = S + L.JC0 + 7 * j;
+      const V3<R> r = parent ? e.ra : e.rb, rg = parent ? e.ra : -e.rb;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        R c = e.C[k] - alpha * c0[k];
+        R f = lam[k] + pen[k] * c;
+        stampLinear(H, g, k, r, s * f, pen[k]);
+        geometric(H, rg, k == 0 ? V3<R>{f, R(0), R(0)} : (k == 1 ? V3<R>{R(0), f, R(0)} : V3<R>{R(0), R(0), f}));
+      }
+#pragma unroll
+      for (int k = 3; k < 5; ++k) {
+        R c = e.C[k] - alpha * c0[k];
+        R f = lam[k] + pen[k] * c;
+        V3<R> t = k == 3 ? e.t1 : e.t2;
+        stampAngular(H, g, cross(t, e.axisB) * s, f, pen[k]);
+        geometric(H, parent ? t : e.axisB, (parent ? e.axisB : t) * f);
+      }
+      // Every remaining row acts along the hinge axis: J = (0, -s axis).
+      R stiff = R(0), force = R(0);
+      if (ldg(m->limited[j])) {
+        R c5 = e.C[5] - alpha * rmin(c0[5], R(0));
+        R f5 = rmin(lam[5] + pen[5] * c5, R(0));
+        if (f5 < R(0)) { stiff += pen[5]; force += f5; }
+        R c6 = e.C[6] - alpha * rmin(c0[6], R(0));
+        R f6 = rmin(lam[6] + pen[6] * c6, R(0));
+        if (f6 < R(0)) { stiff += pen[6]; force -= f6; }
+      }
+      R drive = kp * wrapAngle(e.angle - S[L.JT + j]) - S[L.JTQ + j];
+      R driveStiffness = kp;
+      if (limit > R(0)) {
+        if (fabs(drive) >= limit) driveStiffness = R(0);
+        drive = rclamp(drive, -limit, limit);
+      }
+      stiff += driveStiffness;
+      force += drive;
+      const R damping = S[L.JD + j], armature = ldg(m->armature[j]);
+      const R delta = wrapAngle(e.angle - S[L.JA0 + j]);
+      const R dstiff = damping / h + armature * ih2;
+      if (dstiff > R(0)) {
+        stiff += dstiff;
+        force += damping / h * delta + armature * ih2 * (delta - h * S[L.JV0 + j]);
+      }
+      const R fl = S[L.JFL + j];
+      if (fl > R(0)) {
+        R trial = S[L.JLF + j] + S[L.JPF + j] * delta;
+        force += rclamp(trial, -fl, fl);
+        if (fabs(trial) < fl) stiff += S[L.JPF + j];
+      }
+      stampAngular(H, g, e.axis * (-s), force, stiff);
+    }
+    // Contacts touching bi, in list order.
+    const int n = I[iCount], nGround = I[iGround];
+    for (int ci = 0; ci < n; ++ci) {
+      const int meta = cmeta(ci);
+      const int body = metaBody(meta), other = metaOther(meta);
+      if (body != bi && other != bi) continue;
+      const R *c = contact(ci);
+      V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
+      if (other < 0) {
+        V3<R> ra = rotate(q, local);
+        V3<R> C = x + ra - V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]};
+        C.z -= alpha * c[cC0];
+        V3<R> f = coneForce(C, c);
+        if (f.z < R(0)) {
+          stampLinear(H, g, 0, ra, f.x, c[cPenalty]);
+          stampLinear(H, g, 1, ra, f.y, c[cPenalty + 1]);
+          stampLinear(H, g, 2, ra, f.z, c[cPenalty + 2]);
+          geometric(H, ra, f);
+        }
+      } else {
+        const R *bs = S + L.CB + 9 * (ci - nGround);
+        V3<R> t1{bs[0], bs[1], bs[2]}, t2{bs[3], bs[4], bs[5]}, nn{bs[6], bs[7], bs[8]};
+        Q4<R> qa = ld4(L.Q + 4 * body), qb = ld4(L.Q + 4 * other);
+        V3<R> ra = rotate(qa, local), rb = rotate(qb, V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]});
+        V3<R> delta = ld3(L.X + 3 * body) + ra - ld3(L.X + 3 * other) - rb;
+        V3<R> C{dot(delta, t1), dot(delta, t2), dot(delta, nn)};
+        C.z -= alpha * c[cC0];
+        const bool isOther = bi == other;
+        const R sign = isOther ? R(-1) : R(1);
+        const V3<R> r = isOther ? rb : ra;
+        V3<R> f = coneForce(C, c);
+        if (f.z < R(0)) {
+          V3<R> e0 = t1 * sign, e1 = t2 * sign, e2 = nn * sign;
+          stampDense(H, g, e0, cross(r, e0), f.x, c[cPenalty]);
+          stampDense(H, g, e1, cross(r, e1), f.y, c[cPenalty + 1]);
+          stampDense(H, g, e2, cross(r, e2), f.z, c[cPenalty + 2]);
+          geometric(H, r, (t1 * f.x + t2 * f.y + nn * f.z) * sign);
+        }
+      }
+    }
+    R st[6];
+    if (!solve(H, g, st)) {
+#pragma unroll
+      for (int i = 0; i < 6; ++i) st[i] = R(NAN);
+    }
+    V3<R> tx{st[0], st[1], st[2]}, rx{st[3], st[4], st[5]};
+    R nt = norm(tx), nr = norm(rx);
+    R scale = rmin(R(1), rmin(R(.1) / rmax(nt, R(1e-30)), R(.25) / rmax(nr, R(1e-30))));
+    st3(L.X + 3 * bi, x + tx * scale);
+    st4(L.Q + 4 * bi, qnormalized(qmul(qexp(rx * scale), q)));
+    return rmax(nt, nr) * scale;
+  }
+
+  // ------------------------------------------------------------ substep
+  struct Diag {
+    R jointError, axisError, penetration;
+    int contacts, iterations;
+    bool converged;
+  };
+
+  __device__ bool step(Diag &diag, R kp, R limit) {
+    const R h = m->dt, alpha = m->alpha, gamma = m->gamma;
+    diag = {R(0), R(0), R(0), 0, 0, false};
+    detectContacts();
+    if (m->np > 0) buildColorLists();
+    if (I[iFailed]) {
+      storeContacts();
+      return false;
+    }
+    const int nb = m->nb, nj = m->nj;
+    const R ag = alpha * gamma;
+    // Joint warm start (kernel.cuh:951-964), one lane per joint.
+    for (int j = team.lane; j < nj; j += T) {
+      JointGeo e;
+      evalJoint(j, e);
+#pragma unroll
+      for (int k = 0; k < 7; ++k) S[L.JC0 + 7 * j + k] = e.C[k];
+      S[L.JA0 + j] = e.angle;
+      S[L.JLF + j] *= ag;
+      S[L.JPF + j] = rclamp(S[L.JPF + j] * gamma, R(1), R(1e7));
+      const int a = ldg(m->ja[j]), b = ldg(m->jb[j]);
+      S[L.JV0 + j] = dot(ld3(L.W + 3 * b) - ld3(L.W + 3 * a), e.axis);
+#pragma unroll
+      for (int k = 0; k < 7; ++k) {
+        S[L.JL + 7 * j + k] *= ag;
+        R p = S[L.JP + 7 * j + k] * gamma;
+        S[L.JP + 7 * j + k] = k < 3 ? rclamp(p, R(1000), R(1e9)) : rclamp(p, R(1), R(1e7));
+      }
+    }
+    team.sync();
+    // Predictor (kernel.cuh:965-976), one lane per body.
+    for (int b = team.lane; b < nb; b += T) {
+      V3<R> x = ld3(L.X + 3 * b);
+      Q4<R> q = ld4(L.Q + 4 * b);
+      st3(L.X0 + 3 * b, x);
+      st4(L.Q0 + 4 * b, q);
+      const R mass = ldg(m->mass[b]);
+      if (mass == R(0)) continue;
+      V3<R> in = mv3(m->inertia[b]);
+      // World inertia R diag(I) R^T at q0 (kept for the whole substep).
+      V3<R> ex = rotate(q, V3<R>{R(1), R(0), R(0)}), ey = rotate(q, V3<R>{R(0), R(1), R(0)}),
+            ez = rotate(q, V3<R>{R(0), R(0), R(1)});
+      R *iw = S + L.IW + 6 * b;
+      iw[0] = in.x * ex.x * ex.x + in.y * ey.x * ey.x + in.z * ez.x * ez.x;
+      iw[1] = in.x * ex.y * ex.y + in.y * ey.y * ey.y + in.z * ez.y * ez.y;
+      iw[2] = in.x * ex.z * ex.z + in.y * ey.z * ey.z + in.z * ez.z * ez.z;
+      iw[3] = in.x * ex.x * ex.y + in.y * ey.x * ey.y + in.z * ez.x * ez.y;
+      iw[4] = in.x * ex.x * ex.z + in.y * ey.x * ey.z + in.z * ez.x * ez.z;
+      iw[5] = in.x * ex.y * ex.z + in.y * ey.y * ey.z + in.z * ez.y * ez.z;
+      V3<R> v = ld3(L.V + 3 * b), w = ld3(L.W + 3 * b);
+      V3<R> grav{m->gravity[0], m->gravity[1], m->gravity[2]};
+      V3<R> xp = x + v * h + (grav + bodyForce(b) * (R(1) / mass)) * (h * h);
+      // Gyroscopic predictor: w + h I^-1 (-(w x I w)), body frame.
+      V3<R> wl = rotateInv(q, w);
+      V3<R> Iwl{in.x * wl.x, in.y * wl.y, in.z * wl.z};
+      V3<R> tl = -cross(wl, Iwl);
+      V3<R> wp = w + rotate(q, V3<R>{tl.x / in.x, tl.y / in.y, tl.z / in.z}) * h;
+      Q4<R> qp = qmul(qexp(wp * h), q);
+      st3(L.XP + 3 * b, xp);
+      st4(L.QP + 4 * b, qp);
+      st3(L.X + 3 * b, xp);
+      st4(L.Q + 4 * b, qp);
+    }
+    team.sync();
+    const int colorCount = m->np > 0 ? I[iColors] : 2;
+    const R tol = m->tolerance;
+    for (int it = 0; it < m->iterations; ++it) {
+      R maxUpdate = R(0);
+      for (int color = 0; color < colorCount; ++color) {
+        int begin, end;
+        if (m->np > 0) {
+          begin = I[L.colorStart + color];
+          end = I[L.colorStart + color + 1];
+        } else {
+          begin = ldg(m->colorStart[color]);
+          end = ldg(m->colorStart[color + 1]);
+        }
+        for (int slot = begin + team.lane; slot < end; slot += T) {
+          const int bi = m->np > 0 ? I[L.colorList + slot] : ldg(m->colorBody[slot]);
+          maxUpdate = rmax(maxUpdate, updateBody(bi, kp, limit));
+        }
+        team.sync();
+      }
+      maxUpdate = team.max(maxUpdate);
+      R error = R(0);
+      // Joint multipliers, penalties and dry friction (kernel.cuh:991-1028).
+      for (int j = team.lane; j < nj; j += T) {
+        JointGeo e;
+        evalJoint(j, e);
+        R *lam = S + L.JL + 7 * j, *pen = S + L.JP + 7 * j;
+        const R *c0 = S + L.JC0 + 7 * j;
+        const int rows = ldg(m->limited[j]) ? 7 : 5;
+        for (int k = 0; k < rows; ++k) {
+          R c = e.C[k] - alpha * (k < 5 ? c0[k] : rmin(c0[k], R(0)));
+          R f = lam[k] + pen[k] * c;
+          lam[k] = k >= 5 ? rmin(f, R(0)) : f;
+          if (k < 5 || f < R(0))
+            pen[k] = rmin(pen[k] + (k < 3 ? m->betaLinear : m->betaAngular) * fabs(c), k < 3 ? R(1e9) : R(1e7));
+          error = rmax(error, k < 5 ? R(fabs(c)) : rmax(R(0), -c));
+        }
+        const R fl = S[L.JFL + j];
+        if (fl > R(0)) {
+          R delta = wrapAngle(e.angle - S[L.JA0 + j]);
+          R trial = S[L.JLF + j] + S[L.JPF + j] * delta;
+          R lf = rclamp(trial, -fl, fl);
+          R pf = S[L.JPF + j];
+          if (fabs(trial) < fl) pf = rmin(pf + m->betaAngular * R(fabs(delta)), R(1e7));
+          S[L.JLF + j] = lf;
+          S[L.JPF + j] = pf;
+          R residual = lf + pf * delta;
+          error = rmax(error, R(fabs(lf - rclamp(residual, -fl, fl))) / pf);
+        }
+      }
+      // Contact multipliers, stick flags and penalties (kernel.cuh:1029-1052).
+      const int n = I[iCount], nGround = I[iGround];
+      for (int ci = team.lane; ci < n; ci += T) {
+        R *c = contact(ci);
+        V3<R> C = contactGap(ci, nGround);
+        V3<R> f = coneForce(C, c);
+        R tx = c[cLambda] + c[cPenalty] * C.x, ty = c[cLambda + 1] + c[cPenalty + 1] * C.y;
+        R trial = sqrt(tx * tx + ty * ty);
+        const R mu = c[cFriction];
+        const bool cone = trial <= -mu * f.z;
+        bool stick = cone && sqrt(C.x * C.x + C.y * C.y) < R(1e-5);
+        int meta = cmeta(ci);
+        cmeta(ci) = (meta & ~(1 << 16)) | (stick ? 1 << 16 : 0);
+        R Ck[3] = {C.x, C.y, C.z}, fk[3] = {f.x, f.y, f.z};
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          c[cLambda + k] = fk[k];
+          if (f.z < R(0) && (k == 2 || cone))
+            c[cPenalty + k] = rmin(c[cPenalty + k] + m->betaLinear * R(fabs(Ck[k])), R(1e9));
+        }
+        error = rmax(error, rmax(R(0), -contactGap(ci, nGround).z));
+      }
+      error = team.max(error);
+      team.sync();
+      diag.iterations = it + 1;
+      diag.converged = maxUpdate < tol && error < tol;
+      if (diag.converged) break;
+    }
+    // Velocity recovery (kernel.cuh:1064-1073).
+    bool bad = false;
+    for (int b = team.lane; b < nb; b += T) {
+      if (!(ldg(m->mass[b]) > R(0))) continue;
+      V3<R> x = ld3(L.X + 3 * b);
+      V3<R> v = (x - ld3(L.X0 + 3 * b)) * (R(1) / h);
+      V3<R> w = qlog(qmul(ld4(L.Q + 4 * b), conj(ld4(L.Q0 + 4 * b)))) * (R(1) / h);
+      st3(L.V + 3 * b, v);
+      st3(L.W + 3 * b, w);
+      if (!isfinite(norm(x) + norm(v) + norm(w))) bad = true;
+    }
+    if (team.any(bad)) {
+      if (team.lane == 0) I[iFailed] = 1;
+      team.sync();
+      storeContacts();
+      return false;
+    }
+    // Diagnostics (kernel.cuh:1074-1093).
+    R je = R(0), ae = R(0), pe = R(0);
+    for (int j = team.lane; j < nj; j += T) {
+      JointGeo e;
+      evalJoint(j, e);
+      je = rmax(je, rmax(R(fabs(e.C[0])), rmax(R(fabs(e.C[1])), R(fabs(e.C[2])))));
+      ae = rmax(ae, rmax(R(fabs(e.C[3])), R(fabs(e.C[4]))));
+    }
+    const int n = I[iCount], nGround = I[iGround];
+    for (int ci = team.lane; ci < n; ci += T) {
+      V3<R> C = contactGap(ci, nGround);
+      pe = rmax(pe, rmax(R(0), -(C.z + alpha * contact(ci)[cC0])));
+    }
+    diag.jointError = team.max(je);
+    diag.axisError = team.max(ae);
+    diag.penetration = team.max(pe);
+    diag.contacts = n;
+    team.sync();
+    storeContacts();
+    return true;
+  }
+
+  // Contact gap C in the contact basis, C.z shifted by -alpha c0 (kernel.cuh:805-827).
+  __device__ __forceinline__ V3<R> contactGap(int ci, int nGround) {
+    const R *c = contact(ci);
+    const int meta = cmeta(ci);
+    const int body = metaBody(meta), other = metaOther(meta);
+    V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
+    V3<R> ra = rotate(ld4(L.Q + 4 * body), local);
+    V3<R> C;
+    if (other < 0) {
+      C = ld3(L.X + 3 * body) + ra - V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]};
+    } else {
+      const R *bs = S + L.CB + 9 * (ci - nGround);
+      V3<R> rb = rotate(ld4(L.Q + 4 * other), V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]});
+      V3<R> delta = ld3(L.X + 3 * body) + ra - ld3(L.X + 3 * other) - rb;
+      C = {dot(delta, V3<R>{bs[0], bs[1], bs[2]}), dot(delta, V3<R>{bs[3], bs[4], bs[5]}),
+           dot(delta, V3<R>{bs[6], bs[7], bs[8]})};
+    }
+    C.z -= m->alpha * c[cC0];
+    return C;
+  }
+
+  // BasicState::advance (kernel.cuh:421-443).
+  __device__ void advance(int substeps, R kp, R limit, Diag &summary) {
+    summary = {R(0), R(0), R(0), 0, 0, true};
+    const R h = m->dt;
+    if (!(h > R(0)) || m->iterations < 1) {
+      if (team.lane == 0) I[iFailed] = 1;
+      team.sync();
+      return;
+    }
+    for (int k = 0; k < substeps; ++k) {
+      Diag d;
+      bool ok = step(d, kp, limit);
+      team.sync();
+      if (!ok || I[iFailed]) break;
+      summary.jointError = rmax(summary.jointError, d.jointError);
+      summary.axisError = rmax(summary.axisError, d.axisError);
+      summary.penetration = rmax(summary.penetration, d.penetration);
+      summary.contacts = summary.contacts > d.contacts ? summary.contacts : d.contacts;
+      summary.converged = summary.converged && d.converged;
+      summary.iterations += d.iterations;
+      // The next substep reads the contacts just stored as its warm-start cache.
+      if (team.lane == 0) I[iPrevCount] = I[iCount];
+      team.sync();
+    }
+  }
+};
+
+// One launch advances every environment: target/forces (step) or motor/forces
+// (step_motor), then `substeps` physics steps with all state on chip.
+template <class R, int T>
+__global__ void __launch_bounds__(32) advanceKernel(const DevModel<R> *__restrict__ model,
+                                                    const R *__restrict__ points, R *records,
+                                                    int recordStride, int count, Layout L,
+                                                    StepArgs args) {
+  extern __shared__ __align__(16) unsigned char smemRaw[];
+  constexpr int teams = 32 / T;
+  const int team = threadIdx.x / T;
+  const int env = blockIdx.x * teams + team;
+  if (env >= count) return;
+  R *S = reinterpret_cast<R *>(smemRaw) + size_t(team) * L.size;
+  R *rec = records + size_t(env) * recordStride;
+  Solver<R, T> s(model, points, S, rec, L);
+  const int nj = model->nj;
+  const int lane = s.team.lane;
+  const R *forces = static_cast<const R *>(args.forces) + 3 * size_t(env);
+  R kp, limit;
+  int failed = int(rec[0]);
+  if (args.motor) {
+    // BasicState::setMotor (kernel.cuh:448-466): kp and the PD cap are zero,
+    // the three channels replace torque, dry friction and damping.
+    const R *motor = static_cast<const R *>(args.motor) + size_t(env) * nj * 3;
+    kp = R(0);
+    limit = R(0);
+    bool bad = false;
+    for (int j = lane; j < nj; j += T) {
+      R t = motor[3 * j], fr = motor[3 * j + 1], dm = motor[3 * j + 2];
+      if (!isfinite(t) || !isfinite(fr) || !isfinite(dm) || fr < R(0) || dm < R(0)) bad = true;
+    }
+    for (int k = lane; k < 3; k += T)
+      if (!isfinite(forces[k])) bad = true;
+    failed |= s.team.any(bad) ? 1 : 0;
+    s.load();
+    s.team.sync();
+    for (int j = lane; j < nj; j += T) {
+      S[L.JTQ + j] = motor[3 * j];
+      S[L.JFL + j] = motor[3 * j + 1];
+      S[L.JD + j] = motor[3 * j + 2];
+    }
+    if (lane == 0) {
+      S[L.F1] = forces[0]; S[L.F1 + 1] = forces[1]; S[L.F1 + 2] = forces[2];
+      s.I[iFailed] = failed;
+    }
+    s.team.sync();
+    typename Solver<R, T>::Diag d{R(0), R(0), R(0), 0, 0, true};
+    bool ran = !failed;
+    if (ran) s.advance(1, kp, limit, d);
+    s.team.sync();
+    s.store(kp, limit);
+    if (ran) s.storeHeader(d.jointError, d.penetration, d.contacts, d.converged, d.axisError, d.iterations);
+    else if (lane == 0) rec[0] = R(1);
+    return;
+  }
+  // extension.cu:87-110: validate, then set the PD targets and gains.
+  const R *target = static_cast<const R *>(args.target) + size_t(env) * nj;
+  bool bad = false;
+  for (int j = lane; j < nj; j += T)
+    if (!isfinite(target[j])) bad = true;
+  for (int k = lane; k < 3; k += T)
+    if (!isfinite(forces[k])) bad = true;
+  if (s.team.any(bad)) failed = 1;
+  if (failed) {
+    if (lane == 0) rec[0] = R(1);
+    return;
+  }
+  kp = R(args.kp);
+  limit = R(args.limit);
+  s.load();
+  s.team.sync();
+  for (int j = lane; j < nj; j += T) {
+    S[L.JT + j] = target[j];
+    S[L.JTQ + j] = ldg(model->torque[j]);
+    S[L.JFL + j] = ldg(model->frictionloss[j]);
+    S[L.JD + j] = ldg(model->damping[j]);
+  }
+  if (lane == 0) {
+    S[L.F1] = forces[0]; S[L.F1 + 1] = forces[1]; S[L.F1 + 2] = forces[2];
+    s.I[iFailed] = 0;
+  }
+  s.team.sync();
+  typename Solver<R, T>::Diag d;
+  s.advance(args.substeps, kp, limit, d);
+  s.team.sync();
+  s.store(kp, limit);
+  s.storeHeader(d.jointError, d.penetration, d.contacts, d.converged, d.axisError, d.iterations);
+}
+
+}  // namespace duckb200

@@ -1,0 +1,131 @@
+/* duck_gym_b200 -- C ABI of the B200 AVBD environment-step library.
+ *
+ * This is the drop-in boundary for the reference's CUDA entry points: the
+ * pybind11 class `_duck_cuda.CudaBatch` defined in src/cuda/extension.cu
+ * (Interface at :160-173, Batch<S> at :187-422, makeBatch at :423-435, module
+ * at :436-452).  The reference binds those methods to torch tensors; here every
+ * entry point takes plain device pointers, element counts and a cudaStream_t,
+ * so any host language can bind it (the Python binding lives in
+ * duck_gym_b200/cuda_batch.py and reproduces the reference's Python API).
+ *
+ * Conventions (same as the reference's Batch, extension.cu:203-213):
+ *  - A batch lives on one device.  Every call runs asynchronously on the
+ *    given stream; calls are serialised across streams by a private event
+ *    (the reference's wait()/record()).  Only duck_batch_create and
+ *    duck_batch_destroy synchronise.
+ *  - Real is float for fp64 == 0 and double for fp64 == 1.  Arrays are dense,
+ *    C-contiguous, on the batch's device, with the shapes given below
+ *    (E envs, B bodies, J joints).
+ *  - Numeric failures never raise: they set the sticky per-env flag exported
+ *    as diag[:, 5], which reset clears (kernel.cuh:382).
+ *  - Argument errors return a nonzero status; duck_last_error() describes
+ *    the most recent one on the calling thread.
+ */
+#ifndef DUCK_B200_H
+#define DUCK_B200_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct duck_batch duck_batch;
+typedef struct CUstream_st *duck_stream; /* == cudaStream_t */
+
+enum { DUCK_OK = 0, DUCK_EINVAL = 1, DUCK_ECUDA = 2, DUCK_EMODEL = 3 };
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *duck_last_error(void);
+
+/* Replaces CudaBatch.__init__ / makeBatch (extension.cu:216-265, 423-435).
+ * Loads a DUCK_MODEL v1/v2 file (solver.cpp:67-174), converts it
+ * (model.hpp:237-360) and initialises num_envs environments.
+ * Requires 0 < num_envs <= 65536, dt > 0 finite, iterations > 0.
+ * specialized requires the 16-body / 14-hinge MicroDuck joint layout
+ * (extension.cu:225-237); shared_memory requires specialized.  Both flags
+ * are accepted for API compatibility: this library always keeps each
+ * environment's working state on chip, so they select no other code path. */
+int duck_batch_create(const char *model_path, int num_envs, double dt, int iterations, int device,
+                      int fp64, int specialized, int shared_memory, duck_stream stream,
+                      duck_batch **out);
+/* Replaces Batch::~Batch (extension.cu:266-272). */
+void duck_batch_destroy(duck_batch *batch);
+
+/* Sizes: out[0] E, out[1] B, out[2] J, out[3] contact bound, out[4] portable
+ * record length (Reals), out[5] fp64, out[6] device, out[7] environments per
+ * CTA, out[8] lanes per environment, out[9] shared bytes per CTA. */
+int duck_batch_info(const duck_batch *batch, int32_t *out);
+/* Joint name i (the reference's joint_names property, extension.cu:416-421). */
+const char *duck_batch_joint_name(const duck_batch *batch, int index);
+
+/* Replaces Batch::reset (extension.cu:273-284, kernel resetStates :29-50).
+ * mask [E] uint8 (bool), q [E,J], roots [E,6] (xyz + rotation vector). */
+int duck_batch_reset(duck_batch *batch, const uint8_t *mask, const void *q, const void *roots,
+                     duck_stream stream);
+
+/* Replaces Batch::step (extension.cu:285-306, kernel advance :78-114):
+ * implicit PD targets [E,J], base forces [E,3], substeps > 0, kp >= 0,
+ * limit >= 0 (0 = uncapped). */
+int duck_batch_step(duck_batch *batch, const void *target, const void *forces, int substeps,
+                    double kp, double limit, duck_stream stream);
+
+/* Replaces Batch::stepMotor (extension.cu:307-320, kernel advanceMotor
+ * :115-127): motor [E,J,3] = (torque, dry-friction budget, viscous damping)
+ * held for one physics step, base forces [E,3]. */
+int duck_batch_step_motor(duck_batch *batch, const void *motor, const void *forces,
+                          duck_stream stream);
+
+/* Replaces Batch::state (extension.cu:321-335, kernel snapshot :128-138):
+ * bodies [E,B,13] (x, q wxyz, v, w), joints [E,J,2] (angle, rate),
+ * diag [E,6] (joint error, penetration, contacts, converged, axis error,
+ * failed). */
+int duck_batch_state(duck_batch *batch, void *bodies, void *joints, void *diag,
+                     duck_stream stream);
+
+/* Replaces Batch::contactForces (extension.cu:336-347): [E,B,3]. */
+int duck_batch_contact_forces(duck_batch *batch, void *out, int ground_only, duck_stream stream);
+/* Replaces Batch::selfContactStats (extension.cu:348-359): [E,2]. */
+int duck_batch_self_contact_stats(duck_batch *batch, void *out, duck_stream stream);
+/* Replaces Batch::contactCounts (extension.cu:360-370): [E,2]. */
+int duck_batch_contact_counts(duck_batch *batch, void *out, duck_stream stream);
+/* Replaces Batch::generalizedLoads (extension.cu:371-384): offset [E,3],
+ * out [E,J,3] = (bias, contact+limit, applied actuator) per hinge. */
+int duck_batch_generalized_loads(duck_batch *batch, const void *offset, void *out,
+                                 duck_stream stream);
+
+/* Replaces Batch::reference (extension.cu:385-415): one environment of the
+ * same model advanced from its initial state on the HOST, for quick checks.
+ * target [J], forces [3], outputs bodies [B,13], joints [J,2], diag [6], all
+ * host pointers.  Unlike the reference (which re-runs its solver on the CPU),
+ * this runs the device kernel on a scratch single-env batch and copies back. */
+int duck_batch_reference(duck_batch *batch, const void *target, const void *forces, int substeps,
+                         double kp, double limit, void *bodies, void *joints, void *diag);
+
+/* No reference counterpart.  Copies environments [first, first + count) to
+ * or from a dense array of portable records ([count, record length] Reals,
+ * device memory); the layout is the one written by oracle/avbd_oracle.cpp:
+ * header 8, bodies B x 16, joints J x 22, contacts bound x 32.  Used to load
+ * one state into both this library and the CPU oracle, and for checkpoints. */
+int duck_batch_export(duck_batch *batch, int first, int count, void *records, duck_stream stream);
+int duck_batch_import(duck_batch *batch, int first, int count, const void *records,
+                      duck_stream stream);
+
+/* No reference counterpart.  Contact keys of one environment copied to the
+ * host: keys [capacity,5] int32 rows (body, shape, feature, other,
+ * otherShape); returns the contact count through *count. */
+int duck_batch_contact_keys(duck_batch *batch, int env, int32_t *keys, int capacity, int *count,
+                            duck_stream stream);
+
+/* No reference counterpart.  Number of kernel launches issued by this batch
+ * since creation (for launch accounting in benchmarks). */
+int64_t duck_batch_launches(const duck_batch *batch);
+
+/* No reference counterpart.  FP32 fused-multiply-add throughput probe used
+ * as the roofline denominator: runs `iterations` dependent FMA chains on
+ * every SM and returns achieved TFLOP/s (2 flops per FMA) in *tflops. */
+int duck_fp32_peak(int device, int iterations, double *tflops, duck_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
