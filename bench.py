@@ -84,24 +84,28 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.lines = []
+        self.lines = []      # (monotonic receive time, csv line)
+        self.window = None   # (start, end) of the timed region
 
-    def __enter__(self):
+    def start(self):
+        """Start sampling; returns once the first sample has arrived."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            deadline = time.monotonic() + 10
+            while not self.lines and time.monotonic() < deadline:
+                time.sleep(0.05)
         except OSError:
             self.proc = None
-        return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
-    def __exit__(self, *exc):
+    def stop(self):
         if self.proc:
             self.proc.terminate()
             try:
@@ -111,9 +115,13 @@ class ClockSampler:
             self.thread.join(timeout=5)
 
     def summary(self):
+        """Samples received while the timed region ran (plus one period)."""
         sm, reasons, sm_max, power = [], set(), None, []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        start, end = self.window or (-1e30, 1e30)
+        for when, line in self.lines:
+            if not (start <= when <= end + 0.15):
+                continue
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -232,7 +240,7 @@ def reference_arm(args, rank, world):
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--steps", type=int, default=400)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--envs", type=int, default=ENVS)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -281,17 +289,21 @@ def main():
                 dist.barrier()
             torch.cuda.synchronize(device)
 
+        clocks = ClockSampler(local)
+        clocks.start()
         launches0 = batch.launches
         barrier()
-        with ClockSampler(local) as clocks:
-            wall0 = time.perf_counter()
-            for k in range(args.steps):
-                flush.zero_()
-                starts[k].record(stream)
-                batch.step(target, forces, SUBSTEPS, kp, limit)
-                ends[k].record(stream)
-            barrier()
-            wall = time.perf_counter() - wall0
+        wall0 = time.perf_counter()
+        t_start = time.monotonic()
+        for k in range(args.steps):
+            flush.zero_()
+            starts[k].record(stream)
+            batch.step(target, forces, SUBSTEPS, kp, limit)
+            ends[k].record(stream)
+        barrier()
+        clocks.window = (t_start, time.monotonic())
+        wall = time.perf_counter() - wall0
+        clocks.stop()
         launches = batch.launches - launches0
         kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
         device_s = sum(kernel_ms) / 1e3

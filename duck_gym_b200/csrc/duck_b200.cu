@@ -8,6 +8,7 @@
 #include "../../include/duck_b200.h"
 #include "aux_kernels.cuh"
 
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <stdexcept>
@@ -28,9 +29,15 @@ void check(cudaError_t e, const char *what) {
 void require(bool c, const char *msg) {
   if (!c) throw std::invalid_argument(msg);
 }
+// Lanes per environment: the smallest power of two (>= 4) holding the largest
+// colour class, unless DUCK_B200_LANES (4, 8, 16 or 32) asks for a wider team.
 int teamSize(int colorMax) {
   int t = 4;
   while (t < colorMax && t < 32) t *= 2;
+  if (const char *env = std::getenv("DUCK_B200_LANES")) {
+    int want = std::atoi(env);
+    if ((want == 4 || want == 8 || want == 16 || want == 32) && want >= t) t = want;
+  }
   return t;
 }
 }  // namespace
@@ -281,7 +288,7 @@ int duck_batch_step_motor(duck_batch *b, const void *motor, const void *forces, 
 
 int duck_batch_state(duck_batch *b, void *bodies, void *joints, void *diag, duck_stream stream) {
   return guarded([&] {
-    require(b && bodies && joints && diag, "Invalid arguments");
+    require(b && bodies && diag && (joints || b->nj == 0), "Invalid arguments");
     DeviceGuard guard(b->device);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     begin(b, s);
@@ -329,7 +336,7 @@ int duck_batch_contact_counts(duck_batch *b, void *out, duck_stream stream) {
 
 int duck_batch_generalized_loads(duck_batch *b, const void *offset, void *out, duck_stream stream) {
   return guarded([&] {
-    require(b && offset && out, "Invalid arguments");
+    require(b && offset && (out || b->nj == 0), "Invalid arguments");
     DeviceGuard guard(b->device);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     begin(b, s);
