@@ -11,6 +11,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -434,6 +435,94 @@ int duck_batch_reference(duck_batch *b, const void *target, const void *forces, 
     check(cudaMemcpy(joints, dJoints, 2 * b->nj * real, cudaMemcpyDeviceToHost), "copy joints");
     check(cudaMemcpy(diag, dDiag, 6 * real, cudaMemcpyDeviceToHost), "copy diag");
     b->launches += one.launches - b->launches;
+  });
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of duck_batch_reference.
+//
+// duck_batch_reference takes its one-environment scratch record and staging
+// buffers from cudaMalloc.  Some callers cannot allocate device memory at the
+// moment they want this check: code running while a stream is being captured
+// into a CUDA graph (allocation is not capturable), code under a memory pool
+// or budget that forbids raw cudaMalloc, and control loops that cannot afford
+// the device-wide synchronisation cudaMalloc/cudaFree imply.  This variant
+// keeps the scratch in a file-scope device array instead.  Every GPU that
+// loads the library holds the array (kStaticScratchBytes) until exit; all
+// calls share it and it keeps the previous call's contents, so the record is
+// cleared on every call, and calls that overlap on the GPU race.
+static constexpr size_t kStaticScratchBytes = 32 * 1024;
+static __device__ __align__(256) unsigned char duckStaticScratch[kStaticScratchBytes];
+
+namespace {
+std::mutex staticScratchMutex;
+void *staticScratchAddress[64] = {};
+
+// Device address of duckStaticScratch on `device` (current), resolved once per
+// device: host code cannot use the symbol itself, which names a host-side
+// stand-in, not device memory.
+void *staticScratch(int device) {
+  require(device >= 0 && device < 64, "Device index out of range");
+  std::lock_guard<std::mutex> lock(staticScratchMutex);
+  if (!staticScratchAddress[device]) {
+    void *ptr = nullptr;
+    check(cudaGetSymbolAddress(&ptr, duckStaticScratch), "cudaGetSymbolAddress");
+    staticScratchAddress[device] = ptr;
+  }
+  return staticScratchAddress[device];
+}
+
+template <class R>
+void referenceStatic(const duck_batch *b, char *scratch, size_t recordBytes, const StepArgs &args, char *dBodies,
+                     char *dJoints, char *dDiag) {
+  const DevModel<R> *m = static_cast<const DevModel<R> *>(b->devModel);
+  const R *pts = static_cast<const R *>(b->points);
+  R *rec = reinterpret_cast<R *>(scratch);
+  const int stride = b->recordStride;
+  check(cudaMemset(scratch, 0, recordBytes), "cudaMemset scratch record");
+  resetKernel<R><<<1, 128>>>(m, rec, stride, 1, nullptr, nullptr, nullptr, 0);
+  switch (b->T) {
+    case 4: advanceKernel<R, 4><<<1, 32, b->smemPerBlock>>>(m, pts, rec, stride, 1, b->layout, args); break;
+    case 8: advanceKernel<R, 8><<<1, 32, b->smemPerBlock>>>(m, pts, rec, stride, 1, b->layout, args); break;
+    case 16: advanceKernel<R, 16><<<1, 32, b->smemPerBlock>>>(m, pts, rec, stride, 1, b->layout, args); break;
+    default: advanceKernel<R, 32><<<1, 32, b->smemPerBlock>>>(m, pts, rec, stride, 1, b->layout, args); break;
+  }
+  snapshotKernel<R><<<1, 64>>>(m, rec, stride, 1, reinterpret_cast<R *>(dBodies), reinterpret_cast<R *>(dJoints),
+                               reinterpret_cast<R *>(dDiag));
+  check(cudaGetLastError(), "static reference launch");
+}
+}  // namespace
+
+extern "C" {
+
+int duck_batch_reference_static(duck_batch *b, const void *target, const void *forces, int substeps, double kp,
+                                 double limit, void *bodies, void *joints, void *diag) {
+  return guarded([&] {
+    require(b && forces && bodies && diag && (target || b->nj == 0) && (joints || b->nj == 0) && substeps > 0,
+            "Invalid CPU reference inputs");
+    require(kp >= 0 && std::isfinite(kp) && limit >= 0 && std::isfinite(limit), "Invalid controls");
+    DeviceGuard guard(b->device);
+    const size_t real = b->fp64 ? 8 : 4;
+    const size_t recordBytes = size_t(b->recordStride) * real;
+    const size_t ioBytes = size_t(b->nj + 3 + 13 * b->nb + 2 * b->nj + 6) * real;
+    if (recordBytes + ioBytes > kStaticScratchBytes)
+      throw std::invalid_argument("Model too large for the static reference scratch: needs " +
+                                  std::to_string(recordBytes + ioBytes) + " bytes, the library reserves " +
+                                  std::to_string(kStaticScratchBytes));
+    char *scratch = static_cast<char *>(staticScratch(b->device));
+    char *io = scratch + recordBytes;
+    char *dTarget = io, *dForces = io + b->nj * real, *dBodies = dForces + 3 * real,
+         *dJoints = dBodies + 13 * b->nb * real, *dDiag = dJoints + 2 * b->nj * real;
+    if (b->nj) check(cudaMemcpy(dTarget, target, b->nj * real, cudaMemcpyHostToDevice), "copy target");
+    check(cudaMemcpy(dForces, forces, 3 * real, cudaMemcpyHostToDevice), "copy forces");
+    StepArgs args{dTarget, dForces, nullptr, substeps, kp, limit};
+    if (b->fp64) referenceStatic<double>(b, scratch, recordBytes, args, dBodies, dJoints, dDiag);
+    else referenceStatic<float>(b, scratch, recordBytes, args, dBodies, dJoints, dDiag);
+    check(cudaMemcpy(bodies, dBodies, 13 * b->nb * real, cudaMemcpyDeviceToHost), "copy bodies");
+    if (b->nj) check(cudaMemcpy(joints, dJoints, 2 * b->nj * real, cudaMemcpyDeviceToHost), "copy joints");
+    check(cudaMemcpy(diag, dDiag, 6 * real, cudaMemcpyDeviceToHost), "copy diag");
   });
 }
 

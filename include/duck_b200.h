@@ -101,6 +101,27 @@ int duck_batch_generalized_loads(duck_batch *batch, const void *offset, void *ou
 int duck_batch_reference(duck_batch *batch, const void *target, const void *forces, int substeps,
                          double kp, double limit, void *bodies, void *joints, void *diag);
 
+/* No counterpart in the reference: an allocation-free duck_batch_reference.
+ * Same arguments, same results.  duck_batch_reference takes its scratch (a
+ * one-environment state record plus staging for inputs and outputs) from
+ * cudaMalloc; this entry point calls no cudaMalloc, cudaFree or allocating
+ * library routine.  It is for callers that cannot allocate device memory:
+ * code running while a stream is captured into a CUDA graph, code under a
+ * memory pool or budget that forbids raw cudaMalloc, and control loops that
+ * cannot take the device-wide synchronisation that cudaMalloc/cudaFree imply.
+ * Its scratch is a file-scope device array of 32 KiB that every GPU loading
+ * the library holds until exit; models whose record and staging need more are
+ * rejected with DUCK_EINVAL and a message giving both sizes (the seed biped
+ * needs 10 KiB in fp32, 20 KiB in fp64).  The first call on a device resolves
+ * the array's device address; make that first call before any stream
+ * capture.  All calls share the array and it keeps the previous call's
+ * contents (each call clears the record before use), so calls that overlap on
+ * the GPU race: serialise them.  Inputs and outputs are host pointers, as for
+ * duck_batch_reference. */
+int duck_batch_reference_static(duck_batch *batch, const void *target, const void *forces,
+                                int substeps, double kp, double limit, void *bodies, void *joints,
+                                void *diag);
+
 /* No reference counterpart.  Copies environments [first, first + count) to
  * or from a dense array of portable records ([count, record length] Reals,
  * device memory); the layout is the one written by oracle/avbd_oracle.cpp:
