@@ -133,3 +133,53 @@ template <class R> __device__ __forceinline__ V3<R> xrotate(Q4<R> q, V3<R> v) {
 }
 
 }  // namespace duckb200
+
+namespace duckb200 {
+// ---------------------------------------------------------------- fast path
+// Approximate reciprocal square root / reciprocal / square root (PTX .approx,
+// a few ulp) for the primal/dual solve, whose parity bound is a tolerance.
+__device__ __forceinline__ float frsqrt(float x) { return rsqrtf(x); }
+__device__ __forceinline__ double frsqrt(double x) { return rsqrt(x); }
+__device__ __forceinline__ float frcp(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ double frcp(double x) { return 1.0 / x; }
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdividef(a, b); }
+__device__ __forceinline__ double fdiv(double a, double b) { return a / b; }
+template <class R> __device__ __forceinline__ R fnorm(V3<R> a) { return fsqrt(dot(a, a)); }
+template <class R> __device__ __forceinline__ Q4<R> fnormalized(Q4<R> q) {
+  R n2 = q.w * q.w + q.x * q.x + q.y * q.y + q.z * q.z;
+  if (!(n2 >= R(1e-30))) return {R(NAN), R(NAN), R(NAN), R(NAN)};
+  R inv = frsqrt(n2);
+  return {q.w * inv, q.x * inv, q.y * inv, q.z * inv};
+}
+// Rotation matrix of a unit quaternion, row major.
+template <class R> __device__ __forceinline__ void quatToMatrix(Q4<R> q, R *m) {
+  R xx = q.x * q.x, yy = q.y * q.y, zz = q.z * q.z, xy = q.x * q.y, xz = q.x * q.z, yz = q.y * q.z;
+  R wx = q.w * q.x, wy = q.w * q.y, wz = q.w * q.z;
+  m[0] = R(1) - R(2) * (yy + zz); m[1] = R(2) * (xy - wz); m[2] = R(2) * (xz + wy);
+  m[3] = R(2) * (xy + wz); m[4] = R(1) - R(2) * (xx + zz); m[5] = R(2) * (yz - wx);
+  m[6] = R(2) * (xz - wy); m[7] = R(2) * (yz + wx); m[8] = R(1) - R(2) * (xx + yy);
+}
+template <class R> __device__ __forceinline__ V3<R> matVec(const R *m, V3<R> v) {
+  return {m[0] * v.x + m[1] * v.y + m[2] * v.z, m[3] * v.x + m[4] * v.y + m[5] * v.z,
+          m[6] * v.x + m[7] * v.y + m[8] * v.z};
+}
+// Exponential map with fast normalisation (kernel.cuh:136-145).
+template <class R> __device__ __forceinline__ Q4<R> fqexp(V3<R> v) {
+  R a2 = dot(v, v), a = fsqrt(a2), s, c;
+  sincosT(a * R(0.5), &s, &c);
+  R k = a < R(1e-8) ? R(0.5) - a2 / R(48) : s * frcp(a);
+  return fnormalized(Q4<R>{c, k * v.x, k * v.y, k * v.z});
+}
+// Logarithm of a (near) unit quaternion (kernel.cuh:146-153).
+template <class R> __device__ __forceinline__ V3<R> fqlog(Q4<R> q) {
+  q = fnormalized(q);
+  if (q.w < R(0)) q = {-q.w, -q.x, -q.y, -q.z};
+  V3<R> v{q.x, q.y, q.z};
+  R s = fnorm(v);
+  return v * (s < R(1e-10) ? R(2) : R(2) * atan2(s, q.w) * frcp(s));
+}
+}  // namespace duckb200

@@ -190,9 +190,8 @@ __device__ __noinline__ int detectPairs(int base, int prevCount) {
       bb = ldg(m->sBody[sb]);
       if (!(ldg(m->mass[ba]) == R(0) && ldg(m->mass[bb]) == R(0))) {
         const R radA = ldg(m->sRadius[sa]), radB = ldg(m->sRadius[sb]);
-        skin = xadd(R(.003), xmul(dt, xadd(xadd(xnorm(xsub(ld3(L.V + 3 * ba), ld3(L.V + 3 * bb))),
-                                                  xmul(xnorm(ld3(L.W + 3 * ba)), radA)),
-                                             xmul(xnorm(ld3(L.W + 3 * bb)), radB))));
+        skin = xadd(R(.003), xmul(dt, xadd(xadd(xnorm(xsub(vel(ba), vel(bb))), xmul(xnorm(omega(ba)), radA)),
+                                             xmul(xnorm(omega(bb)), radB))));
         if (!(xnorm(xsub(ld3(L.X + 3 * ba), ld3(L.X + 3 * bb))) > xadd(xadd(radA, radB), skin)))
           hit = xconvexContact(sa, sb, skin, tolerance);
       }
@@ -231,8 +230,7 @@ __device__ __noinline__ int detectPairs(int base, int prevCount) {
           break;
         }
         R *c = contact(slot);
-        cmeta(slot) = ba | ((bb + 1) << 8);
-        ckey(slot) = sa | ((sb + 1) << 16);
+        cmeta(slot) = packMeta(ba, bb, sa, sb);
         cfeat(slot) = 0;
         c[cLocal] = local.x; c[cLocal + 1] = local.y; c[cLocal + 2] = local.z;
         c[cAnchor] = localB.x; c[cAnchor + 1] = localB.y; c[cAnchor + 2] = localB.z;

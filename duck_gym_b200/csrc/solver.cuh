@@ -11,10 +11,14 @@
 //    warm start, predictor, contact construction and velocity recovery on
 //    lane 0; here every phase is spread over the team (a lane per body, joint,
 //    shape or contact), and 4 environments share a warp;
+//  * each body keeps its rotation matrix on chip, so every hinge and contact
+//    lever is a 9-FMA product; each body also keeps a bit mask of the contacts
+//    that touch it;
 //  * the primal update of a body exploits the structure of each Jacobian row
-//    (unit-axis linear rows, pure angular rows) and assembles only the lower
-//    triangle of the 6x6 block; all hinge-axis terms (limits, PD drive,
-//    damping, dry friction) are summed into one rank-one update;
+//    (unit-axis linear rows, pure angular rows), forms the geometric-stiffness
+//    majorizer of the unit-axis rows in closed form, assembles only the lower
+//    triangle of the 6x6 block, and sums every hinge-axis term (limits, PD
+//    drive, damping, dry friction) into one rank-one update;
 //  * the frozen world inertia of a body is formed once per substep;
 //  * contact generation reproduces the reference's arithmetic bit for bit
 //    (x-prefixed ops of dmath.cuh) so contact sets match the CPU exactly.
@@ -26,20 +30,19 @@ namespace duckb200 {
 
 // Portable record: header 8, bodies B x 16, joints J x 22, contacts bound x 32.
 constexpr int kRecHeader = 8, kRecBody = 16, kRecJoint = 22, kRecContact = 32;
-// On-chip contact entry: meta, keys, feature, local(3), anchor/localB(3),
-// friction, c0, lambda(3), penalty(3).
-constexpr int kC = 17;
-enum { cMeta = 0, cKey = 1, cFeature = 2, cLocal = 3, cAnchor = 6, cFriction = 9, cC0 = 10,
-       cLambda = 11, cPenalty = 14 };
+// On-chip contact entry (16 words): packed keys, feature, local(3),
+// anchor or localB(3), friction, c0, lambda(3), penalty(3).
+constexpr int kC = 16;
+enum { cMeta = 0, cFeature = 1, cLocal = 2, cAnchor = 5, cFriction = 8, cC0 = 9, cLambda = 10, cPenalty = 13 };
 // Team-shared integers.
 enum { iFailed = 0, iCount = 1, iGround = 2, iColors = 3, iPrevCount = 4, iMisc = 8 };
 
 struct Layout {
-  int X, Q, XP, QP, X0, Q0, V, W, IW, F1, KP;          // bodies, base force, kp/limit
+  int X, Q, RM, XQP, X0, Q0, IW, F1;                   // bodies (XQP: v,w between substeps, x~,q~ inside)
   int JL, JP, JC0, JA0, JV0, JLF, JPF, JT, JTQ, JFL, JD;  // joints
   int C, CB;                                           // contacts, self-contact basis
   int I;                                               // ints (Real slot offset)
-  int colors, colorList, colorStart;                   // offsets inside the int region
+  int colors, colorList, colorStart, masks;            // offsets inside the int region
   int cap, pairCap, maxColors;
   int size;                                            // Reals per environment
 };
@@ -49,9 +52,8 @@ template <class R> __host__ inline Layout makeLayout(const DevModel<R> &m) {
   int o = 0;
   auto take = [&](int n) { int at = o; o += n; return at; };
   const int nb = m.nb, nj = m.nj;
-  L.X = take(3 * nb); L.Q = take(4 * nb); L.XP = take(3 * nb); L.QP = take(4 * nb);
-  L.X0 = take(3 * nb); L.Q0 = take(4 * nb); L.V = take(3 * nb); L.W = take(3 * nb);
-  L.IW = take(6 * nb); L.F1 = take(3); L.KP = take(2);
+  L.X = take(3 * nb); L.Q = take(4 * nb); L.RM = take(9 * nb); L.XQP = take(7 * nb);
+  L.X0 = take(3 * nb); L.Q0 = take(4 * nb); L.IW = take(6 * nb); L.F1 = take(3);
   L.JL = take(7 * nj); L.JP = take(7 * nj); L.JC0 = take(7 * nj); L.JA0 = take(nj);
   L.JV0 = take(nj); L.JLF = take(nj); L.JPF = take(nj); L.JT = take(nj); L.JTQ = take(nj);
   L.JFL = take(nj); L.JD = take(nj);
@@ -60,10 +62,11 @@ template <class R> __host__ inline Layout makeLayout(const DevModel<R> &m) {
   L.C = take(kC * std::max(L.cap, 1));
   L.CB = take(9 * std::max(L.pairCap, 1));
   L.maxColors = 2 + m.np;
-  int ints = iMisc + nb + nb + L.maxColors + 1;
   L.colors = iMisc;
   L.colorList = iMisc + nb;
   L.colorStart = iMisc + 2 * nb;
+  L.masks = L.colorStart + L.maxColors + 1;
+  int ints = L.masks + 2 * nb;
   L.I = take(int((ints * sizeof(int) + sizeof(R) - 1) / sizeof(R)));
   // Pad so consecutive environments start on different banks.
   int padded = (o + 3) & ~3;
@@ -134,17 +137,32 @@ template <class R, int T> struct Solver {
   __device__ __forceinline__ void st4(int off, Q4<R> q) { S[off] = q.w; S[off + 1] = q.x; S[off + 2] = q.y; S[off + 3] = q.z; }
   __device__ __forceinline__ V3<R> mv3(const R (&a)[3]) const { return {ldg(a[0]), ldg(a[1]), ldg(a[2])}; }
   __device__ __forceinline__ Q4<R> mq4(const R (&a)[4]) const { return {ldg(a[0]), ldg(a[1]), ldg(a[2]), ldg(a[3])}; }
+  __device__ __forceinline__ const R *rot(int b) const { return S + L.RM + 9 * b; }
+  __device__ __forceinline__ void setPose(int b, V3<R> x, Q4<R> q) {
+    st3(L.X + 3 * b, x);
+    st4(L.Q + 4 * b, q);
+    quatToMatrix(q, S + L.RM + 9 * b);
+  }
+  // Velocities live in the XQP slots between substeps (predicted poses inside).
+  __device__ __forceinline__ V3<R> vel(int b) const { return ld3(L.XQP + 7 * b); }
+  __device__ __forceinline__ V3<R> omega(int b) const { return ld3(L.XQP + 7 * b + 3); }
   __device__ __forceinline__ V3<R> bodyForce(int b) const {
     return b == 1 ? ld3(L.F1) : V3<R>{R(0), R(0), R(0)};
   }
   __device__ __forceinline__ R *contact(int c) { return S + L.C + kC * c; }
+  __device__ __forceinline__ const R *contact(int c) const { return S + L.C + kC * c; }
   __device__ __forceinline__ int &cmeta(int c) { return reinterpret_cast<int &>(S[L.C + kC * c + cMeta]); }
-  __device__ __forceinline__ int &ckey(int c) { return reinterpret_cast<int &>(S[L.C + kC * c + cKey]); }
+  __device__ __forceinline__ int cmeta(int c) const { return reinterpret_cast<const int &>(S[L.C + kC * c + cMeta]); }
   __device__ __forceinline__ int &cfeat(int c) { return reinterpret_cast<int &>(S[L.C + kC * c + cFeature]); }
-  // meta: body | (other + 1) << 8 | stick << 16
-  __device__ static __forceinline__ int metaBody(int meta) { return meta & 0xff; }
-  __device__ static __forceinline__ int metaOther(int meta) { return ((meta >> 8) & 0xff) - 1; }
-  __device__ static __forceinline__ bool metaStick(int meta) { return (meta >> 16) & 1; }
+  // meta: body (5 bits) | other + 1 (6) | stick (1) | shape (5) | otherShape + 1 (6)
+  __device__ static __forceinline__ int packMeta(int body, int other, int shape, int otherShape) {
+    return body | ((other + 1) << 5) | (shape << 12) | ((otherShape + 1) << 17);
+  }
+  __device__ static __forceinline__ int metaBody(int meta) { return meta & 31; }
+  __device__ static __forceinline__ int metaOther(int meta) { return ((meta >> 5) & 63) - 1; }
+  __device__ static __forceinline__ bool metaStick(int meta) { return (meta >> 11) & 1; }
+  __device__ static __forceinline__ int metaShape(int meta) { return (meta >> 12) & 31; }
+  __device__ static __forceinline__ int metaOtherShape(int meta) { return ((meta >> 17) & 63) - 1; }
 
   // ------------------------------------------------------------ load / store
   // Record -> shared memory.  Contacts stay in the record: the first
@@ -153,10 +171,9 @@ template <class R, int T> struct Solver {
     const int nb = m->nb, nj = m->nj;
     for (int b = team.lane; b < nb; b += T) {
       const R *r = rec + kRecHeader + kRecBody * b;
-      st3(L.X + 3 * b, {r[0], r[1], r[2]});
-      st4(L.Q + 4 * b, {r[3], r[4], r[5], r[6]});
-      st3(L.V + 3 * b, {r[7], r[8], r[9]});
-      st3(L.W + 3 * b, {r[10], r[11], r[12]});
+      setPose(b, {r[0], r[1], r[2]}, {r[3], r[4], r[5], r[6]});
+      R *vw = S + L.XQP + 7 * b;
+      vw[0] = r[7]; vw[1] = r[8]; vw[2] = r[9]; vw[3] = r[10]; vw[4] = r[11]; vw[5] = r[12];
     }
     for (int j = team.lane; j < nj; j += T) {
       const R *r = rec + kRecHeader + kRecBody * nb + kRecJoint * j;
@@ -180,13 +197,13 @@ template <class R, int T> struct Solver {
       I[iCount] = 0;
     }
   }
-  // Shared memory -> record (bodies, joints, header); contacts are written at
-  // the end of every substep.
+  // Shared memory -> record (bodies, joints); contacts are written at the
+  // end of every substep and the header by storeHeader.
   __device__ void store(R kp, R limit) {
     const int nb = m->nb, nj = m->nj;
     for (int b = team.lane; b < nb; b += T) {
       R *r = rec + kRecHeader + kRecBody * b;
-      V3<R> x = ld3(L.X + 3 * b), v = ld3(L.V + 3 * b), w = ld3(L.W + 3 * b);
+      V3<R> x = ld3(L.X + 3 * b), v = vel(b), w = omega(b);
       Q4<R> q = ld4(L.Q + 4 * b);
       r[0] = x.x; r[1] = x.y; r[2] = x.z; r[3] = q.w; r[4] = q.x; r[5] = q.y; r[6] = q.z;
       r[7] = v.x; r[8] = v.y; r[9] = v.z; r[10] = w.x; r[11] = w.y; r[12] = w.z;
@@ -218,10 +235,10 @@ template <class R, int T> struct Solver {
     for (int c = team.lane; c < n; c += T) {
       const R *s = contact(c);
       R *r = base + kRecContact * c;
-      int meta = cmeta(c), key = ckey(c);
-      int other = metaOther(meta);
-      r[0] = R(metaBody(meta)); r[1] = R(key & 0xffff); r[2] = R(cfeat(c)); r[3] = R(other);
-      r[4] = R((key >> 16) - 1); r[5] = R(metaStick(meta) ? 1 : 0);
+      const int meta = cmeta(c);
+      const int other = metaOther(meta);
+      r[0] = R(metaBody(meta)); r[1] = R(metaShape(meta)); r[2] = R(cfeat(c)); r[3] = R(other);
+      r[4] = R(metaOtherShape(meta)); r[5] = R(metaStick(meta) ? 1 : 0);
       r[6] = s[cLocal]; r[7] = s[cLocal + 1]; r[8] = s[cLocal + 2];
       if (other < 0) {
         r[9] = s[cAnchor]; r[10] = s[cAnchor + 1]; r[11] = s[cAnchor + 2];
@@ -263,7 +280,7 @@ template <class R, int T> struct Solver {
     const R mass = ldg(m->mass[b]);
     if (!m->ground || !ldg(m->sGround[s]) || mass == R(0)) return 0;
     const R dt = m->dt;
-    V3<R> x = ld3(L.X + 3 * b), v = ld3(L.V + 3 * b), w = ld3(L.W + 3 * b);
+    V3<R> x = ld3(L.X + 3 * b), v = vel(b), w = omega(b);
     Q4<R> q = ld4(L.Q + 4 * b);
     const R accel = xadd(m->gravity[2], bodyForce(b).z / mass);
     const R dt2 = xmul(dt, dt);
@@ -277,8 +294,8 @@ template <class R, int T> struct Solver {
       V3<R> bestWorld{};
       for (int k = 0; k < count; ++k) {
         V3<R> local = xpoint(s, q, k), wp = xadd(x, xrotate(q, local));
-        V3<R> vel = xadd(v, xcross(w, xsub(wp, x)));
-        R z = rmin(wp.z, xadd(xadd(wp.z, xmul(dt, vel.z)), xmul(dt2, accel)));
+        V3<R> vv = xadd(v, xcross(w, xsub(wp, x)));
+        R z = rmin(wp.z, xadd(xadd(wp.z, xmul(dt, vv.z)), xmul(dt2, accel)));
         if (double(z) >= .003 || z >= lowest) continue;
         bool duplicate = false;
         for (int c = 0; c < n; ++c)
@@ -319,8 +336,7 @@ template <class R, int T> struct Solver {
     const R c0 = rmin(xadd(x, xrotate(q, local)).z, R(0));
     const R ag = xmul(m->alpha, m->gamma);
     R *c = contact(slot);
-    cmeta(slot) = b | (0 << 8);
-    ckey(slot) = s | (0 << 16);
+    cmeta(slot) = packMeta(b, -1, s, -1);
     cfeat(slot) = best;
     c[cLocal] = local.x; c[cLocal + 1] = local.y; c[cLocal + 2] = local.z;
     c[cAnchor] = anchor.x; c[cAnchor + 1] = anchor.y; c[cAnchor + 2] = anchor.z;
@@ -361,6 +377,19 @@ template <class R, int T> struct Solver {
     if (m->np > 0) base = detectPairs(base, prevCount);
     if (team.lane == 0) I[iCount] = base;
     team.sync();
+    // Per-body masks of the contacts touching each body (list order).
+    if (L.cap <= 64) {
+      for (int b = team.lane; b < nb; b += T) {
+        unsigned long long mask = 0ull;
+        for (int c = 0; c < base; ++c) {
+          const int meta = cmeta(c);
+          if (metaBody(meta) == b || metaOther(meta) == b) mask |= 1ull << c;
+        }
+        I[L.masks + 2 * b] = int(unsigned(mask));
+        I[L.masks + 2 * b + 1] = int(unsigned(mask >> 32));
+      }
+      team.sync();
+    }
   }
 
   // Colour lists of the dynamic bodies; contacts between equal colours move
@@ -385,21 +414,22 @@ template <class R, int T> struct Solver {
     R C[7];
     R angle;
   };
+  // Hinge constraint values and world frames (kernel.cuh:725-761).
   __device__ __forceinline__ void evalJoint(int j, JointGeo &e) const {
     const int a = ldg(m->ja[j]), b = ldg(m->jb[j]);
-    Q4<R> qa = ld4(L.Q + 4 * a), qb = ld4(L.Q + 4 * b);
+    const R *Ra = rot(a), *Rb = rot(b);
     V3<R> xa = ld3(L.X + 3 * a), xb = ld3(L.X + 3 * b);
-    e.ra = rotate(qa, mv3(m->ra[j]));
-    e.rb = rotate(qb, mv3(m->rb[j]));
+    e.ra = matVec(Ra, mv3(m->ra[j]));
+    e.rb = matVec(Rb, mv3(m->rb[j]));
     V3<R> d = xa + e.ra - xb - e.rb;
     e.C[0] = d.x; e.C[1] = d.y; e.C[2] = d.z;
-    e.axis = rotate(qa, mv3(m->axisA[j]));
-    e.axisB = rotate(qb, mv3(m->axisB[j]));
-    e.t1 = rotate(qa, mv3(m->tangentA[j]));
+    e.axis = matVec(Ra, mv3(m->axisA[j]));
+    e.axisB = matVec(Rb, mv3(m->axisB[j]));
+    e.t1 = matVec(Ra, mv3(m->tangentA[j]));
     e.t2 = cross(e.axis, e.t1);
     e.C[3] = dot(e.t1, e.axisB);
     e.C[4] = dot(e.t2, e.axisB);
-    V3<R> u = rotate(qb, mv3(m->tangentB[j]));
+    V3<R> u = matVec(Rb, mv3(m->tangentB[j]));
     e.angle = atan2(dot(e.axis, cross(e.t1, u)), dot(e.t1, u));
     e.C[5] = e.angle - ldg(m->lo[j]);
     e.C[6] = ldg(m->hi[j]) - e.angle;
@@ -439,7 +469,8 @@ template <class R, int T> struct Solver {
       for (int k = 0; k <= i; ++k) H[tri(i, k)] += pj * J[k];
     }
   }
-  // Diagonal majorizer of the rotational geometric stiffness (kernel.cuh:283-301).
+  // Diagonal majorizer of the rotational geometric stiffness of force f at
+  // lever r: column norms of (r f^T + f r^T) / 2 - (r.f) I (kernel.cuh:283-301).
   static __device__ __forceinline__ void geometric(R *H, V3<R> r, V3<R> f) {
     R rf = dot(r, f);
     R a00 = r.x * f.x - rf, a11 = r.y * f.y - rf, a22 = r.z * f.z - rf;
@@ -450,14 +481,24 @@ template <class R, int T> struct Solver {
     H[tri(4, 4)] += fsqrt(a01 * a01 + a11 * a11 + a12 * a12);
     H[tri(5, 5)] += fsqrt(a02 * a02 + a12 * a12 + a22 * a22);
   }
+  // The same majorizer summed over three unit-axis forces f_k e_k at one
+  // lever: for f along e_k the column norms are |f_k| times square roots of
+  // quadratic forms of r alone.
+  static __device__ __forceinline__ void geometricAxes(R *H, V3<R> r, R f0, R f1, R f2) {
+    const R x2 = r.x * r.x, y2 = r.y * r.y, z2 = r.z * r.z;
+    const R a0 = fabs(f0), a1 = fabs(f1), a2 = fabs(f2);
+    H[tri(3, 3)] += a0 * R(0.5) * fsqrt(y2 + z2) + a1 * fsqrt(y2 + R(0.25) * x2) + a2 * fsqrt(z2 + R(0.25) * x2);
+    H[tri(4, 4)] += a0 * fsqrt(x2 + R(0.25) * y2) + a1 * R(0.5) * fsqrt(x2 + z2) + a2 * fsqrt(z2 + R(0.25) * y2);
+    H[tri(5, 5)] += a0 * fsqrt(x2 + R(0.25) * z2) + a1 * fsqrt(y2 + R(0.25) * z2) + a2 * R(0.5) * fsqrt(x2 + y2);
+  }
   // Friction-cone clamped contact force (kernel.cuh:304-315).
   static __device__ __forceinline__ V3<R> coneForce(V3<R> C, const R *c) {
     V3<R> f{c[cLambda] + c[cPenalty] * C.x, c[cLambda + 1] + c[cPenalty + 1] * C.y,
             c[cLambda + 2] + c[cPenalty + 2] * C.z};
     f.z = rmin(f.z, R(0));
-    R t = sqrt(f.x * f.x + f.y * f.y), bound = -c[cFriction] * f.z;
-    if (t > bound && t > R(0)) {
-      R s = bound / t;
+    R t2 = f.x * f.x + f.y * f.y, bound = -c[cFriction] * f.z;
+    if (t2 > bound * bound && t2 > R(0)) {
+      R s = bound * frsqrt(t2);
       f.x *= s;
       f.y *= s;
     }
@@ -478,7 +519,7 @@ template <class R, int T> struct Solver {
     return (R(1) - h * c / s) / (a * a);
   }
   // Solve H x = -g with a packed Cholesky factorisation (kernel.cuh:177-228);
-  // NaN on a non-positive pivot.
+  // false on a non-positive pivot.
   static __device__ __forceinline__ bool solve(const R *H, const R *g, R *x) {
     R Lf[21], inv[6];
 #pragma unroll
@@ -490,9 +531,9 @@ template <class R, int T> struct Solver {
         for (int k = 0; k < j; ++k) v -= Lf[tri(i, k)] * Lf[tri(j, k)];
         if (i == j) {
           if (!(v > R(0)) || !isfinite(v)) return false;
-          R l = sqrt(v);
-          Lf[tri(i, i)] = l;
-          inv[i] = R(1) / l;
+          R r = frsqrt(v);
+          Lf[tri(i, i)] = v * r;
+          inv[i] = r;
         } else {
           Lf[tri(i, j)] = v * inv[j];
         }
@@ -520,22 +561,22 @@ template <class R, int T> struct Solver {
   // Block update of body bi (kernel.cuh:828-936).
   __device__ R updateBody(int bi, R kp, R limit) {
     const R h = m->dt, alpha = m->alpha;
-    const R ih2 = R(1) / (h * h);
+    const R ih = R(1) / h, ih2 = ih * ih;
     const R mass = ldg(m->mass[bi]);
     R H[21], g[6];
 #pragma unroll
     for (int i = 0; i < 21; ++i) H[i] = R(0);
 #pragma unroll
     for (int i = 0; i < 6; ++i) g[i] = R(0);
-    V3<R> x = ld3(L.X + 3 * bi), xp = ld3(L.XP + 3 * bi);
-    Q4<R> q = ld4(L.Q + 4 * bi), qp = ld4(L.QP + 4 * bi);
+    const V3<R> x = ld3(L.X + 3 * bi), xp = ld3(L.XQP + 7 * bi);
+    const Q4<R> q = ld4(L.Q + 4 * bi), qp = ld4(L.XQP + 7 * bi + 3);
     // Inertia block with the SO(3) log Jacobian and frozen world inertia.
     {
-      V3<R> dx = x - xp, th = qlog(qmul(q, conj(qp)));
+      V3<R> dx = x - xp, th = fqlog(qmul(q, conj(qp)));
       R ml = mass * ih2;
       H[tri(0, 0)] = ml; H[tri(1, 1)] = ml; H[tri(2, 2)] = ml;
       g[0] = ml * dx.x; g[1] = ml * dx.y; g[2] = ml * dx.z;
-      R a2 = dot(th, th), a = sqrt(a2);
+      R a2 = dot(th, th), a = fsqrt(a2);
       R coef = logJacobianCoef(a);
       // rotJ[k] = e_k - theta x e_k / 2 + coef theta x (theta x e_k), as columns.
       R J[3][3];
@@ -576,14 +617,18 @@ template <class R, int T> struct Solver {
       const bool parent = ldg(m->ja[j]) == bi;
       const R s = parent ? R(1) : R(-1);
       const R *lam = S + L.JL + 7 * j, *pen = S + L.JP + 7 * j, *c0 = S + L.JC0 + 7 * j;
-      const V3<R> r = parent ? e.ra : e.rb, rg = parent ? e.ra : -e.rb;
+      const V3<R> r = parent ? e.ra : e.rb;
+      R f3[3];
 #pragma unroll
       for (int k = 0; k < 3; ++k) {
         R c = e.C[k] - alpha * c0[k];
         R f = lam[k] + pen[k] * c;
+        f3[k] = f;
         stampLinear(H, g, k, r, s * f, pen[k]);
-        geometric(H, rg, k == 0 ? V3<R>{f, R(0), R(0)} : (k == 1 ? V3<R>{R(0), f, R(0)} : V3<R>{R(0), R(0), f}));
       }
+      // Anchor rows: lever (parent ? ra : -rb) under unit-axis forces f_k e_k;
+      // the majorizer depends on the lever only through its squares.
+      geometricAxes(H, r, f3[0], f3[1], f3[2]);
 #pragma unroll
       for (int k = 3; k < 5; ++k) {
         R c = e.C[k] - alpha * c0[k];
@@ -612,10 +657,10 @@ template <class R, int T> struct Solver {
       force += drive;
       const R damping = S[L.JD + j], armature = ldg(m->armature[j]);
       const R delta = wrapAngle(e.angle - S[L.JA0 + j]);
-      const R dstiff = damping / h + armature * ih2;
+      const R dstiff = damping * ih + armature * ih2;
       if (dstiff > R(0)) {
         stiff += dstiff;
-        force += damping / h * delta + armature * ih2 * (delta - h * S[L.JV0 + j]);
+        force += damping * ih * delta + armature * ih2 * (delta - h * S[L.JV0 + j]);
       }
       const R fl = S[L.JFL + j];
       if (fl > R(0)) {
@@ -626,15 +671,15 @@ template <class R, int T> struct Solver {
       stampAngular(H, g, e.axis * (-s), force, stiff);
     }
     // Contacts touching bi, in list order.
-    const int n = I[iCount], nGround = I[iGround];
-    for (int ci = 0; ci < n; ++ci) {
+    const int nGround = I[iGround];
+    const R *Rb = rot(bi);
+    auto touch = [&](int ci) {
       const int meta = cmeta(ci);
       const int body = metaBody(meta), other = metaOther(meta);
-      if (body != bi && other != bi) continue;
       const R *c = contact(ci);
       V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
       if (other < 0) {
-        V3<R> ra = rotate(q, local);
+        V3<R> ra = matVec(Rb, local);
         V3<R> C = x + ra - V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]};
         C.z -= alpha * c[cC0];
         V3<R> f = coneForce(C, c);
@@ -647,8 +692,7 @@ template <class R, int T> struct Solver {
       } else {
         const R *bs = S + L.CB + 9 * (ci - nGround);
         V3<R> t1{bs[0], bs[1], bs[2]}, t2{bs[3], bs[4], bs[5]}, nn{bs[6], bs[7], bs[8]};
-        Q4<R> qa = ld4(L.Q + 4 * body), qb = ld4(L.Q + 4 * other);
-        V3<R> ra = rotate(qa, local), rb = rotate(qb, V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]});
+        V3<R> ra = matVec(rot(body), local), rb = matVec(rot(other), V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]});
         V3<R> delta = ld3(L.X + 3 * body) + ra - ld3(L.X + 3 * other) - rb;
         V3<R> C{dot(delta, t1), dot(delta, t2), dot(delta, nn)};
         C.z -= alpha * c[cC0];
@@ -664,6 +708,20 @@ template <class R, int T> struct Solver {
           geometric(H, r, (t1 * f.x + t2 * f.y + nn * f.z) * sign);
         }
       }
+    };
+    if (L.cap <= 64) {
+      unsigned long long mask = unsigned(I[L.masks + 2 * bi]) | (unsigned long long)unsigned(I[L.masks + 2 * bi + 1]) << 32;
+      while (mask) {
+        const int ci = __ffsll((long long)mask) - 1;
+        mask &= mask - 1;
+        touch(ci);
+      }
+    } else {
+      const int n = I[iCount];
+      for (int ci = 0; ci < n; ++ci) {
+        const int meta = cmeta(ci);
+        if (metaBody(meta) == bi || metaOther(meta) == bi) touch(ci);
+      }
     }
     R st[6];
     if (!solve(H, g, st)) {
@@ -671,11 +729,31 @@ template <class R, int T> struct Solver {
       for (int i = 0; i < 6; ++i) st[i] = R(NAN);
     }
     V3<R> tx{st[0], st[1], st[2]}, rx{st[3], st[4], st[5]};
-    R nt = norm(tx), nr = norm(rx);
-    R scale = rmin(R(1), rmin(R(.1) / rmax(nt, R(1e-30)), R(.25) / rmax(nr, R(1e-30))));
-    st3(L.X + 3 * bi, x + tx * scale);
-    st4(L.Q + 4 * bi, qnormalized(qmul(qexp(rx * scale), q)));
+    R nt = fnorm(tx), nr = fnorm(rx);
+    R scale = rmin(R(1), rmin(R(.1) * frcp(rmax(nt, R(1e-30))), R(.25) * frcp(rmax(nr, R(1e-30)))));
+    setPose(bi, x + tx * scale, fnormalized(qmul(fqexp(rx * scale), q)));
     return rmax(nt, nr) * scale;
+  }
+
+  // Contact gap C in the contact basis, C.z shifted by -alpha c0 (kernel.cuh:805-827).
+  __device__ __forceinline__ V3<R> contactGap(int ci, int nGround) const {
+    const R *c = contact(ci);
+    const int meta = cmeta(ci);
+    const int body = metaBody(meta), other = metaOther(meta);
+    V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
+    V3<R> ra = matVec(rot(body), local);
+    V3<R> C;
+    if (other < 0) {
+      C = ld3(L.X + 3 * body) + ra - V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]};
+    } else {
+      const R *bs = S + L.CB + 9 * (ci - nGround);
+      V3<R> rb = matVec(rot(other), V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]});
+      V3<R> delta = ld3(L.X + 3 * body) + ra - ld3(L.X + 3 * other) - rb;
+      C = {dot(delta, V3<R>{bs[0], bs[1], bs[2]}), dot(delta, V3<R>{bs[3], bs[4], bs[5]}),
+           dot(delta, V3<R>{bs[6], bs[7], bs[8]})};
+    }
+    C.z -= m->alpha * c[cC0];
+    return C;
   }
 
   // ------------------------------------------------------------ substep
@@ -706,7 +784,7 @@ template <class R, int T> struct Solver {
       S[L.JLF + j] *= ag;
       S[L.JPF + j] = rclamp(S[L.JPF + j] * gamma, R(1), R(1e7));
       const int a = ldg(m->ja[j]), b = ldg(m->jb[j]);
-      S[L.JV0 + j] = dot(ld3(L.W + 3 * b) - ld3(L.W + 3 * a), e.axis);
+      S[L.JV0 + j] = dot(omega(b) - omega(a), e.axis);
 #pragma unroll
       for (int k = 0; k < 7; ++k) {
         S[L.JL + 7 * j + k] *= ag;
@@ -715,7 +793,8 @@ template <class R, int T> struct Solver {
       }
     }
     team.sync();
-    // Predictor (kernel.cuh:965-976), one lane per body.
+    // Predictor (kernel.cuh:965-976), one lane per body.  The predicted pose
+    // takes over the velocity slots of the body.
     for (int b = team.lane; b < nb; b += T) {
       V3<R> x = ld3(L.X + 3 * b);
       Q4<R> q = ld4(L.Q + 4 * b);
@@ -725,8 +804,8 @@ template <class R, int T> struct Solver {
       if (mass == R(0)) continue;
       V3<R> in = mv3(m->inertia[b]);
       // World inertia R diag(I) R^T at q0 (kept for the whole substep).
-      V3<R> ex = rotate(q, V3<R>{R(1), R(0), R(0)}), ey = rotate(q, V3<R>{R(0), R(1), R(0)}),
-            ez = rotate(q, V3<R>{R(0), R(0), R(1)});
+      const R *Rm = rot(b);
+      V3<R> ex{Rm[0], Rm[3], Rm[6]}, ey{Rm[1], Rm[4], Rm[7]}, ez{Rm[2], Rm[5], Rm[8]};
       R *iw = S + L.IW + 6 * b;
       iw[0] = in.x * ex.x * ex.x + in.y * ey.x * ey.x + in.z * ez.x * ez.x;
       iw[1] = in.x * ex.y * ex.y + in.y * ey.y * ey.y + in.z * ez.y * ez.y;
@@ -734,19 +813,20 @@ template <class R, int T> struct Solver {
       iw[3] = in.x * ex.x * ex.y + in.y * ey.x * ey.y + in.z * ez.x * ez.y;
       iw[4] = in.x * ex.x * ex.z + in.y * ey.x * ey.z + in.z * ez.x * ez.z;
       iw[5] = in.x * ex.y * ex.z + in.y * ey.y * ey.z + in.z * ez.y * ez.z;
-      V3<R> v = ld3(L.V + 3 * b), w = ld3(L.W + 3 * b);
+      V3<R> v = vel(b), w = omega(b);
       V3<R> grav{m->gravity[0], m->gravity[1], m->gravity[2]};
       V3<R> xp = x + v * h + (grav + bodyForce(b) * (R(1) / mass)) * (h * h);
       // Gyroscopic predictor: w + h I^-1 (-(w x I w)), body frame.
-      V3<R> wl = rotateInv(q, w);
+      V3<R> wl{Rm[0] * w.x + Rm[3] * w.y + Rm[6] * w.z, Rm[1] * w.x + Rm[4] * w.y + Rm[7] * w.z,
+               Rm[2] * w.x + Rm[5] * w.y + Rm[8] * w.z};
       V3<R> Iwl{in.x * wl.x, in.y * wl.y, in.z * wl.z};
       V3<R> tl = -cross(wl, Iwl);
-      V3<R> wp = w + rotate(q, V3<R>{tl.x / in.x, tl.y / in.y, tl.z / in.z}) * h;
-      Q4<R> qp = qmul(qexp(wp * h), q);
-      st3(L.XP + 3 * b, xp);
-      st4(L.QP + 4 * b, qp);
-      st3(L.X + 3 * b, xp);
-      st4(L.Q + 4 * b, qp);
+      V3<R> wp = w + matVec(Rm, V3<R>{tl.x / in.x, tl.y / in.y, tl.z / in.z}) * h;
+      Q4<R> qp = qmul(fqexp(wp * h), q);
+      R *xqp = S + L.XQP + 7 * b;
+      xqp[0] = xp.x; xqp[1] = xp.y; xqp[2] = xp.z;
+      xqp[3] = qp.w; xqp[4] = qp.x; xqp[5] = qp.y; xqp[6] = qp.z;
+      setPose(b, xp, qp);
     }
     team.sync();
     const int colorCount = m->np > 0 ? I[iColors] : 2;
@@ -795,22 +875,22 @@ template <class R, int T> struct Solver {
           S[L.JLF + j] = lf;
           S[L.JPF + j] = pf;
           R residual = lf + pf * delta;
-          error = rmax(error, R(fabs(lf - rclamp(residual, -fl, fl))) / pf);
+          error = rmax(error, R(fabs(lf - rclamp(residual, -fl, fl))) * frcp(pf));
         }
       }
       // Contact multipliers, stick flags and penalties (kernel.cuh:1029-1052).
       const int n = I[iCount], nGround = I[iGround];
       for (int ci = team.lane; ci < n; ci += T) {
         R *c = contact(ci);
-        V3<R> C = contactGap(ci, nGround);
+        const V3<R> C = contactGap(ci, nGround);
         V3<R> f = coneForce(C, c);
         R tx = c[cLambda] + c[cPenalty] * C.x, ty = c[cLambda + 1] + c[cPenalty + 1] * C.y;
-        R trial = sqrt(tx * tx + ty * ty);
+        R trial = fsqrt(tx * tx + ty * ty);
         const R mu = c[cFriction];
         const bool cone = trial <= -mu * f.z;
-        bool stick = cone && sqrt(C.x * C.x + C.y * C.y) < R(1e-5);
-        int meta = cmeta(ci);
-        cmeta(ci) = (meta & ~(1 << 16)) | (stick ? 1 << 16 : 0);
+        const bool stick = cone && C.x * C.x + C.y * C.y < R(1e-10);
+        const int meta = cmeta(ci);
+        cmeta(ci) = (meta & ~(1 << 11)) | (stick ? 1 << 11 : 0);
         R Ck[3] = {C.x, C.y, C.z}, fk[3] = {f.x, f.y, f.z};
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
@@ -818,7 +898,7 @@ template <class R, int T> struct Solver {
           if (f.z < R(0) && (k == 2 || cone))
             c[cPenalty + k] = rmin(c[cPenalty + k] + m->betaLinear * R(fabs(Ck[k])), R(1e9));
         }
-        error = rmax(error, rmax(R(0), -contactGap(ci, nGround).z));
+        error = rmax(error, rmax(R(0), -C.z));
       }
       error = team.max(error);
       team.sync();
@@ -826,16 +906,17 @@ template <class R, int T> struct Solver {
       diag.converged = maxUpdate < tol && error < tol;
       if (diag.converged) break;
     }
-    // Velocity recovery (kernel.cuh:1064-1073).
+    // Velocity recovery (kernel.cuh:1064-1073); the velocities return to the
+    // XQP slots.
     bool bad = false;
     for (int b = team.lane; b < nb; b += T) {
       if (!(ldg(m->mass[b]) > R(0))) continue;
       V3<R> x = ld3(L.X + 3 * b);
       V3<R> v = (x - ld3(L.X0 + 3 * b)) * (R(1) / h);
-      V3<R> w = qlog(qmul(ld4(L.Q + 4 * b), conj(ld4(L.Q0 + 4 * b)))) * (R(1) / h);
-      st3(L.V + 3 * b, v);
-      st3(L.W + 3 * b, w);
-      if (!isfinite(norm(x) + norm(v) + norm(w))) bad = true;
+      V3<R> w = fqlog(qmul(ld4(L.Q + 4 * b), conj(ld4(L.Q0 + 4 * b)))) * (R(1) / h);
+      R *vw = S + L.XQP + 7 * b;
+      vw[0] = v.x; vw[1] = v.y; vw[2] = v.z; vw[3] = w.x; vw[4] = w.y; vw[5] = w.z;
+      if (!isfinite(dot(x, x) + dot(v, v) + dot(w, w))) bad = true;
     }
     if (team.any(bad)) {
       if (team.lane == 0) I[iFailed] = 1;
@@ -863,27 +944,6 @@ template <class R, int T> struct Solver {
     team.sync();
     storeContacts();
     return true;
-  }
-
-  // Contact gap C in the contact basis, C.z shifted by -alpha c0 (kernel.cuh:805-827).
-  __device__ __forceinline__ V3<R> contactGap(int ci, int nGround) {
-    const R *c = contact(ci);
-    const int meta = cmeta(ci);
-    const int body = metaBody(meta), other = metaOther(meta);
-    V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
-    V3<R> ra = rotate(ld4(L.Q + 4 * body), local);
-    V3<R> C;
-    if (other < 0) {
-      C = ld3(L.X + 3 * body) + ra - V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]};
-    } else {
-      const R *bs = S + L.CB + 9 * (ci - nGround);
-      V3<R> rb = rotate(ld4(L.Q + 4 * other), V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]});
-      V3<R> delta = ld3(L.X + 3 * body) + ra - ld3(L.X + 3 * other) - rb;
-      C = {dot(delta, V3<R>{bs[0], bs[1], bs[2]}), dot(delta, V3<R>{bs[3], bs[4], bs[5]}),
-           dot(delta, V3<R>{bs[6], bs[7], bs[8]})};
-    }
-    C.z -= m->alpha * c[cC0];
-    return C;
   }
 
   // BasicState::advance (kernel.cuh:421-443).
