@@ -163,7 +163,7 @@ template <class R> __device__ __forceinline__ void quatToMatrix(Q4<R> q, R *m) {
   m[3] = R(2) * (xy + wz); m[4] = R(1) - R(2) * (xx + zz); m[5] = R(2) * (yz - wx);
   m[6] = R(2) * (xz - wy); m[7] = R(2) * (yz + wx); m[8] = R(1) - R(2) * (xx + yy);
 }
-template <class R> __device__ __forceinline__ V3<R> matVec(const R *m, V3<R> v) {
+template <class M, class R> __device__ __forceinline__ V3<R> matVec(const M &m, V3<R> v) {
   return {m[0] * v.x + m[1] * v.y + m[2] * v.z, m[3] * v.x + m[4] * v.y + m[5] * v.z,
           m[6] * v.x + m[7] * v.y + m[8] * v.z};
 }

@@ -42,6 +42,10 @@ template <class R> struct DevModel {
   R lo[kMaxJoints], hi[kMaxJoints], damping[kMaxJoints], armature[kMaxJoints];
   R frictionloss[kMaxJoints], torque[kMaxJoints], kp[kMaxJoints], target[kMaxJoints];
   R maxTorque[kMaxJoints];
+  // Hot copies for the step kernel, laid out for 128-bit loads: per joint
+  // (a, b, limited, 0) and ra, rb, axisA, axisB, tangentA, tangentB, lo, hi.
+  alignas(16) int jInfo[kMaxJoints][4];
+  alignas(16) R jFrame[kMaxJoints][20];
   // shapes
   int sBody[kMaxShapes], sType[kMaxShapes], sOffset[kMaxShapes], sCount[kMaxShapes];
   int sGround[kMaxShapes];
@@ -250,6 +254,12 @@ HostModel<R> convertModel(const ParsedModel &o, double dt, int iterations, bool 
     d.lo[i] = R(j.lo); d.hi[i] = R(j.hi); d.limited[i] = j.limited; d.damping[i] = R(j.damping);
     d.armature[i] = R(j.armature); d.frictionloss[i] = R(j.frictionloss); d.torque[i] = R(j.torque);
     d.kp[i] = R(j.kp); d.target[i] = R(j.target); d.maxTorque[i] = R(j.maxTorque);
+    d.jInfo[i][0] = j.a; d.jInfo[i][1] = j.b; d.jInfo[i][2] = j.limited; d.jInfo[i][3] = 0;
+    for (int k = 0; k < 3; ++k) {
+      d.jFrame[i][k] = d.ra[i][k]; d.jFrame[i][3 + k] = d.rb[i][k]; d.jFrame[i][6 + k] = d.axisA[i][k];
+      d.jFrame[i][9 + k] = d.axisB[i][k]; d.jFrame[i][12 + k] = d.tangentA[i][k]; d.jFrame[i][15 + k] = d.tangentB[i][k];
+    }
+    d.jFrame[i][18] = d.lo[i]; d.jFrame[i][19] = d.hi[i];
     h.jointNames.push_back(j.name);
   }
   for (auto &j : o.joints)

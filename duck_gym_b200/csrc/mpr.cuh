@@ -10,7 +10,7 @@ struct Sup { V3<R> v, a, b; };
 struct Hit { int status; V3<R> normal, position; R depth; };
 
 __device__ V3<R> xsupport(int s, int body, V3<R> d, R inflation) const {
-  const Q4<R> q = ld4(L.Q + 4 * body);
+  const Q4<R> q = quat(body);
   const V3<R> x = ld3(L.X + 3 * body);
   V3<R> ldir = xrotate(conj(q), d), local;
   const int type = ldg(m->sType[s]);
@@ -103,8 +103,8 @@ __device__ __noinline__ Hit xconvexContact(int sa, int sb, R inflation, R tolera
   Hit result{0, {R(0), R(0), R(0)}, {R(0), R(0), R(0)}, R(0)};
   const int ba = ldg(m->sBody[sa]), bb = ldg(m->sBody[sb]);
   Sup p[4];
-  p[0].a = xadd(ld3(L.X + 3 * ba), xrotate(ld4(L.Q + 4 * ba), mv3(m->sInterior[sa])));
-  p[0].b = xadd(ld3(L.X + 3 * bb), xrotate(ld4(L.Q + 4 * bb), mv3(m->sInterior[sb])));
+  p[0].a = xadd(ld3(L.X + 3 * ba), xrotate(quat(ba), mv3(m->sInterior[sa])));
+  p[0].b = xadd(ld3(L.X + 3 * bb), xrotate(quat(bb), mv3(m->sInterior[sb])));
   p[0].v = xsub(p[0].a, p[0].b);
   const R scale = rmax(R(.001), xadd(ldg(m->sRadius[sa]), ldg(m->sRadius[sb])));
   const R epsilon = xmul(tolerance, R(.01));
@@ -204,7 +204,7 @@ __device__ __noinline__ int detectPairs(int base, int prevCount) {
       if (slot >= L.cap) {
         I[iFailed] = 1;
       } else {
-        const Q4<R> qa = ld4(L.Q + 4 * ba), qb = ld4(L.Q + 4 * bb);
+        const Q4<R> qa = quat(ba), qb = quat(bb);
         const V3<R> n = hit.normal;
         const V3<R> ax = fabs(n.x) < R(.8) ? V3<R>{R(1), R(0), R(0)} : V3<R>{R(0), R(1), R(0)};
         const V3<R> t1 = xunit(xcross(ax, n));
@@ -229,7 +229,7 @@ __device__ __noinline__ int detectPairs(int base, int prevCount) {
           penalty[0] = o[29]; penalty[1] = o[30]; penalty[2] = o[31];
           break;
         }
-        R *c = contact(slot);
+        SV c = contact(slot);
         cmeta(slot) = packMeta(ba, bb, sa, sb);
         cfeat(slot) = 0;
         c[cLocal] = local.x; c[cLocal + 1] = local.y; c[cLocal + 2] = local.z;
@@ -241,7 +241,7 @@ __device__ __noinline__ int detectPairs(int base, int prevCount) {
           c[cLambda + d] = xmul(lambda[d], ag);
           c[cPenalty + d] = rclamp(xmul(penalty[d], m->gamma), R(1000), R(1e9));
         }
-        R *bs = S + L.CB + 9 * (slot - nGround);
+        SV bs = S + (L.CB + 9 * (slot - nGround));
         bs[0] = t1.x; bs[1] = t1.y; bs[2] = t1.z;
         bs[3] = t2.x; bs[4] = t2.y; bs[5] = t2.z;
         bs[6] = n.x; bs[7] = n.y; bs[8] = n.z;

@@ -20,6 +20,10 @@
 //    triangle of the 6x6 block, and sums every hinge-axis term (limits, PD
 //    drive, damping, dry friction) into one rank-one update;
 //  * the frozen world inertia of a body is formed once per substep;
+//  * the four environments of a warp are interleaved word by word in shared
+//    memory (element i of team t at word 4 i + t) and every per-body and
+//    per-contact stride is odd, so lanes of different teams never share a
+//    bank and lanes of one team rarely do;
 //  * contact generation reproduces the reference's arithmetic bit for bit
 //    (x-prefixed ops of dmath.cuh) so contact sets match the CPU exactly.
 #pragma once
@@ -30,15 +34,19 @@ namespace duckb200 {
 
 // Portable record: header 8, bodies B x 16, joints J x 22, contacts bound x 32.
 constexpr int kRecHeader = 8, kRecBody = 16, kRecJoint = 22, kRecContact = 32;
-// On-chip contact entry (16 words): packed keys, feature, local(3),
-// anchor or localB(3), friction, c0, lambda(3), penalty(3).
-constexpr int kC = 16;
+// On-chip contact entry (17 words, odd for conflict-free lane-strided
+// access): packed keys, feature, local(3), anchor or localB(3), friction, c0,
+// lambda(3), penalty(3), padding.
+constexpr int kC = 17;
 enum { cMeta = 0, cFeature = 1, cLocal = 2, cAnchor = 5, cFriction = 8, cC0 = 9, cLambda = 10, cPenalty = 13 };
 // Team-shared integers.
 enum { iFailed = 0, iCount = 1, iGround = 2, iColors = 3, iPrevCount = 4, iMisc = 8 };
 
+// Strides of the per-body arrays (odd: see the interleaving note above).
+constexpr int kSQ = 5, kSIW = 7;
+
 struct Layout {
-  int X, Q, RM, XQP, X0, Q0, IW, F1;                   // bodies (XQP: v,w between substeps, x~,q~ inside)
+  int X, Q, RM, XQP, IW, F1;                           // bodies (XQP: v,w between substeps, x~,q~ inside)
   int JL, JP, JC0, JA0, JV0, JLF, JPF, JT, JTQ, JFL, JD;  // joints
   int C, CB;                                           // contacts, self-contact basis
   int I;                                               // ints (Real slot offset)
@@ -52,8 +60,8 @@ template <class R> __host__ inline Layout makeLayout(const DevModel<R> &m) {
   int o = 0;
   auto take = [&](int n) { int at = o; o += n; return at; };
   const int nb = m.nb, nj = m.nj;
-  L.X = take(3 * nb); L.Q = take(4 * nb); L.RM = take(9 * nb); L.XQP = take(7 * nb);
-  L.X0 = take(3 * nb); L.Q0 = take(4 * nb); L.IW = take(6 * nb); L.F1 = take(3);
+  L.X = take(3 * nb); L.Q = take(kSQ * nb); L.RM = take(9 * nb); L.XQP = take(7 * nb);
+  L.IW = take(kSIW * nb); L.F1 = take(3);
   L.JL = take(7 * nj); L.JP = take(7 * nj); L.JC0 = take(7 * nj); L.JA0 = take(nj);
   L.JV0 = take(nj); L.JLF = take(nj); L.JPF = take(nj); L.JT = take(nj); L.JTQ = take(nj);
   L.JFL = take(nj); L.JD = take(nj);
@@ -66,16 +74,24 @@ template <class R> __host__ inline Layout makeLayout(const DevModel<R> &m) {
   L.colorList = iMisc + nb;
   L.colorStart = iMisc + 2 * nb;
   L.masks = L.colorStart + L.maxColors + 1;
-  int ints = L.masks + 2 * nb;
-  L.I = take(int((ints * sizeof(int) + sizeof(R) - 1) / sizeof(R)));
-  // Pad so consecutive environments start on different banks.
-  int padded = (o + 3) & ~3;
-  if ((padded % 32) == 0) padded += 4;
-  L.size = padded;
+  // One Real slot per integer keeps the interleaved addressing uniform.
+  L.I = take(L.masks + 2 * nb);
+  L.size = o;
   return L;
 }
 
 template <class T> __device__ __forceinline__ T ldg(const T &v) { return __ldg(&v); }
+
+// A team's view of the interleaved shared block: element i at p[i * STRIDE].
+template <class R, int STRIDE> struct View {
+  R *p;
+  __device__ __forceinline__ R &operator[](int i) const { return p[i * STRIDE]; }
+  __device__ __forceinline__ View operator+(int i) const { return {p + i * STRIDE}; }
+};
+template <class R, int STRIDE> struct IntView {
+  R *p;
+  __device__ __forceinline__ int &operator[](int i) const { return reinterpret_cast<int &>(p[i * STRIDE]); }
+};
 
 template <int T> struct Team {
   unsigned mask;
@@ -117,17 +133,20 @@ struct StepArgs {
 };
 
 template <class R, int T> struct Solver {
+  static constexpr int kTeams = 32 / T;
+  static constexpr int kPerLane = (kMaxBodies + T - 1) / T;   // bodies per lane in lane-per-body loops
+  using SV = View<R, kTeams>;
   const DevModel<R> *__restrict__ m;
   const R *__restrict__ pts;
-  R *S;        // environment's shared-memory block
-  int *I;      // its integer region
-  R *rec;      // environment's global record
+  SV S;                    // environment's interleaved shared-memory view
+  IntView<R, kTeams> I;    // its integer region
+  R *rec;                  // environment's global record
   const Layout &L;
   Team<T> team;
 
-  __device__ Solver(const DevModel<R> *model, const R *points, R *smem, R *record, const Layout &layout)
-      : m(model), pts(points), S(smem), rec(record), L(layout) {
-    I = reinterpret_cast<int *>(S + L.I);
+  __device__ Solver(const DevModel<R> *model, const R *points, R *smemTeam, R *record, const Layout &layout)
+      : m(model), pts(points), S{smemTeam}, rec(record), L(layout) {
+    I = IntView<R, kTeams>{smemTeam + size_t(L.I) * kTeams};
   }
 
   // ------------------------------------------------------------ accessors
@@ -137,11 +156,15 @@ template <class R, int T> struct Solver {
   __device__ __forceinline__ void st4(int off, Q4<R> q) { S[off] = q.w; S[off + 1] = q.x; S[off + 2] = q.y; S[off + 3] = q.z; }
   __device__ __forceinline__ V3<R> mv3(const R (&a)[3]) const { return {ldg(a[0]), ldg(a[1]), ldg(a[2])}; }
   __device__ __forceinline__ Q4<R> mq4(const R (&a)[4]) const { return {ldg(a[0]), ldg(a[1]), ldg(a[2]), ldg(a[3])}; }
-  __device__ __forceinline__ const R *rot(int b) const { return S + L.RM + 9 * b; }
+  __device__ __forceinline__ SV rot(int b) const { return S + (L.RM + 9 * b); }
+  __device__ __forceinline__ Q4<R> quat(int b) const { return ld4(L.Q + kSQ * b); }
   __device__ __forceinline__ void setPose(int b, V3<R> x, Q4<R> q) {
     st3(L.X + 3 * b, x);
-    st4(L.Q + 4 * b, q);
-    quatToMatrix(q, S + L.RM + 9 * b);
+    st4(L.Q + kSQ * b, q);
+    R mm[9];
+    quatToMatrix(q, mm);
+#pragma unroll
+    for (int k = 0; k < 9; ++k) S[L.RM + 9 * b + k] = mm[k];
   }
   // Velocities live in the XQP slots between substeps (predicted poses inside).
   __device__ __forceinline__ V3<R> vel(int b) const { return ld3(L.XQP + 7 * b); }
@@ -149,11 +172,10 @@ template <class R, int T> struct Solver {
   __device__ __forceinline__ V3<R> bodyForce(int b) const {
     return b == 1 ? ld3(L.F1) : V3<R>{R(0), R(0), R(0)};
   }
-  __device__ __forceinline__ R *contact(int c) { return S + L.C + kC * c; }
-  __device__ __forceinline__ const R *contact(int c) const { return S + L.C + kC * c; }
-  __device__ __forceinline__ int &cmeta(int c) { return reinterpret_cast<int &>(S[L.C + kC * c + cMeta]); }
-  __device__ __forceinline__ int cmeta(int c) const { return reinterpret_cast<const int &>(S[L.C + kC * c + cMeta]); }
-  __device__ __forceinline__ int &cfeat(int c) { return reinterpret_cast<int &>(S[L.C + kC * c + cFeature]); }
+  __device__ __forceinline__ SV contact(int c) const { return S + (L.C + kC * c); }
+  __device__ __forceinline__ int &cmeta(int c) const { return reinterpret_cast<int &>(S[L.C + kC * c + cMeta]); }
+
+  __device__ __forceinline__ int &cfeat(int c) const { return reinterpret_cast<int &>(S[L.C + kC * c + cFeature]); }
   // meta: body (5 bits) | other + 1 (6) | stick (1) | shape (5) | otherShape + 1 (6)
   __device__ static __forceinline__ int packMeta(int body, int other, int shape, int otherShape) {
     return body | ((other + 1) << 5) | (shape << 12) | ((otherShape + 1) << 17);
@@ -172,7 +194,7 @@ template <class R, int T> struct Solver {
     for (int b = team.lane; b < nb; b += T) {
       const R *r = rec + kRecHeader + kRecBody * b;
       setPose(b, {r[0], r[1], r[2]}, {r[3], r[4], r[5], r[6]});
-      R *vw = S + L.XQP + 7 * b;
+      SV vw = S + (L.XQP + 7 * b);
       vw[0] = r[7]; vw[1] = r[8]; vw[2] = r[9]; vw[3] = r[10]; vw[4] = r[11]; vw[5] = r[12];
     }
     for (int j = team.lane; j < nj; j += T) {
@@ -204,7 +226,7 @@ template <class R, int T> struct Solver {
     for (int b = team.lane; b < nb; b += T) {
       R *r = rec + kRecHeader + kRecBody * b;
       V3<R> x = ld3(L.X + 3 * b), v = vel(b), w = omega(b);
-      Q4<R> q = ld4(L.Q + 4 * b);
+      Q4<R> q = quat(b);
       r[0] = x.x; r[1] = x.y; r[2] = x.z; r[3] = q.w; r[4] = q.x; r[5] = q.y; r[6] = q.z;
       r[7] = v.x; r[8] = v.y; r[9] = v.z; r[10] = w.x; r[11] = w.y; r[12] = w.z;
       if (b == 1) { V3<R> f = ld3(L.F1); r[13] = f.x; r[14] = f.y; r[15] = f.z; }
@@ -233,7 +255,7 @@ template <class R, int T> struct Solver {
     const int n = I[iCount], nGround = I[iGround];
     R *base = rec + kRecHeader + kRecBody * m->nb + kRecJoint * m->nj;
     for (int c = team.lane; c < n; c += T) {
-      const R *s = contact(c);
+      const SV s = contact(c);
       R *r = base + kRecContact * c;
       const int meta = cmeta(c);
       const int other = metaOther(meta);
@@ -246,7 +268,7 @@ template <class R, int T> struct Solver {
         r[15] = R(1); r[16] = R(0); r[17] = R(0); r[18] = R(0); r[19] = R(1); r[20] = R(0);
         r[21] = R(0); r[22] = R(0); r[23] = R(1);
       } else {
-        const R *bs = S + L.CB + 9 * (c - nGround);
+        const SV bs = S + (L.CB + 9 * (c - nGround));
         r[9] = r[10] = r[11] = R(0);
         r[12] = s[cAnchor]; r[13] = s[cAnchor + 1]; r[14] = s[cAnchor + 2];
 #pragma unroll
@@ -281,7 +303,7 @@ template <class R, int T> struct Solver {
     if (!m->ground || !ldg(m->sGround[s]) || mass == R(0)) return 0;
     const R dt = m->dt;
     V3<R> x = ld3(L.X + 3 * b), v = vel(b), w = omega(b);
-    Q4<R> q = ld4(L.Q + 4 * b);
+    Q4<R> q = quat(b);
     const R accel = xadd(m->gravity[2], bodyForce(b).z / mass);
     const R dt2 = xmul(dt, dt);
     R low = rmin(x.z, xadd(xadd(x.z, xmul(dt, v.z)), xmul(dt2, accel)));
@@ -316,7 +338,7 @@ template <class R, int T> struct Solver {
   __device__ void buildGround(int slot, int s, int best, V3<R> bestWorld, int prevCount) {
     const int b = ldg(m->sBody[s]);
     V3<R> x = ld3(L.X + 3 * b);
-    Q4<R> q = ld4(L.Q + 4 * b);
+    Q4<R> q = quat(b);
     V3<R> local = xpoint(s, q, best);
     V3<R> anchor{bestWorld.x, bestWorld.y, R(0)};
     R lambda[3] = {R(0), R(0), R(0)}, penalty[3] = {R(1000), R(1000), R(1000)};
@@ -335,7 +357,7 @@ template <class R, int T> struct Solver {
     }
     const R c0 = rmin(xadd(x, xrotate(q, local)).z, R(0));
     const R ag = xmul(m->alpha, m->gamma);
-    R *c = contact(slot);
+    SV c = contact(slot);
     cmeta(slot) = packMeta(b, -1, s, -1);
     cfeat(slot) = best;
     c[cLocal] = local.x; c[cLocal + 1] = local.y; c[cLocal + 2] = local.z;
@@ -413,26 +435,50 @@ template <class R, int T> struct Solver {
     V3<R> ra, rb, axis, axisB, t1, t2;
     R C[7];
     R angle;
+    int a, b, limited;
   };
+  // ra, rb, axisA, axisB, tangentA, tangentB, lo, hi of joint j in 128-bit loads.
+  __device__ __forceinline__ void loadFrame(int j, R (&f)[20]) const {
+    if constexpr (sizeof(R) == 4) {
+      const float4 *src = reinterpret_cast<const float4 *>(m->jFrame[j]);
+#pragma unroll
+      for (int k = 0; k < 5; ++k) {
+        float4 v = __ldg(src + k);
+        f[4 * k] = v.x; f[4 * k + 1] = v.y; f[4 * k + 2] = v.z; f[4 * k + 3] = v.w;
+      }
+    } else {
+      const double2 *src = reinterpret_cast<const double2 *>(m->jFrame[j]);
+#pragma unroll
+      for (int k = 0; k < 10; ++k) {
+        double2 v = __ldg(src + k);
+        f[2 * k] = v.x; f[2 * k + 1] = v.y;
+      }
+    }
+  }
   // Hinge constraint values and world frames (kernel.cuh:725-761).
   __device__ __forceinline__ void evalJoint(int j, JointGeo &e) const {
-    const int a = ldg(m->ja[j]), b = ldg(m->jb[j]);
-    const R *Ra = rot(a), *Rb = rot(b);
-    V3<R> xa = ld3(L.X + 3 * a), xb = ld3(L.X + 3 * b);
-    e.ra = matVec(Ra, mv3(m->ra[j]));
-    e.rb = matVec(Rb, mv3(m->rb[j]));
+    const int4 info = __ldg(reinterpret_cast<const int4 *>(m->jInfo[j]));
+    e.a = info.x;
+    e.b = info.y;
+    e.limited = info.z;
+    R f[20];
+    loadFrame(j, f);
+    const SV Ra = rot(e.a), Rb = rot(e.b);
+    V3<R> xa = ld3(L.X + 3 * e.a), xb = ld3(L.X + 3 * e.b);
+    e.ra = matVec(Ra, V3<R>{f[0], f[1], f[2]});
+    e.rb = matVec(Rb, V3<R>{f[3], f[4], f[5]});
     V3<R> d = xa + e.ra - xb - e.rb;
     e.C[0] = d.x; e.C[1] = d.y; e.C[2] = d.z;
-    e.axis = matVec(Ra, mv3(m->axisA[j]));
-    e.axisB = matVec(Rb, mv3(m->axisB[j]));
-    e.t1 = matVec(Ra, mv3(m->tangentA[j]));
+    e.axis = matVec(Ra, V3<R>{f[6], f[7], f[8]});
+    e.axisB = matVec(Rb, V3<R>{f[9], f[10], f[11]});
+    e.t1 = matVec(Ra, V3<R>{f[12], f[13], f[14]});
     e.t2 = cross(e.axis, e.t1);
     e.C[3] = dot(e.t1, e.axisB);
     e.C[4] = dot(e.t2, e.axisB);
-    V3<R> u = matVec(Rb, mv3(m->tangentB[j]));
+    V3<R> u = matVec(Rb, V3<R>{f[15], f[16], f[17]});
     e.angle = atan2(dot(e.axis, cross(e.t1, u)), dot(e.t1, u));
-    e.C[5] = e.angle - ldg(m->lo[j]);
-    e.C[6] = ldg(m->hi[j]) - e.angle;
+    e.C[5] = e.angle - f[18];
+    e.C[6] = f[19] - e.angle;
   }
 
   // ------------------------------------------------------------ 6x6 algebra
@@ -492,7 +538,7 @@ template <class R, int T> struct Solver {
     H[tri(5, 5)] += a0 * fsqrt(x2 + R(0.25) * z2) + a1 * fsqrt(y2 + R(0.25) * z2) + a2 * R(0.5) * fsqrt(x2 + y2);
   }
   // Friction-cone clamped contact force (kernel.cuh:304-315).
-  static __device__ __forceinline__ V3<R> coneForce(V3<R> C, const R *c) {
+  static __device__ __forceinline__ V3<R> coneForce(V3<R> C, SV c) {
     V3<R> f{c[cLambda] + c[cPenalty] * C.x, c[cLambda + 1] + c[cPenalty + 1] * C.y,
             c[cLambda + 2] + c[cPenalty + 2] * C.z};
     f.z = rmin(f.z, R(0));
@@ -569,7 +615,7 @@ template <class R, int T> struct Solver {
 #pragma unroll
     for (int i = 0; i < 6; ++i) g[i] = R(0);
     const V3<R> x = ld3(L.X + 3 * bi), xp = ld3(L.XQP + 7 * bi);
-    const Q4<R> q = ld4(L.Q + 4 * bi), qp = ld4(L.XQP + 7 * bi + 3);
+    const Q4<R> q = quat(bi), qp = ld4(L.XQP + 7 * bi + 3);
     // Inertia block with the SO(3) log Jacobian and frozen world inertia.
     {
       V3<R> dx = x - xp, th = fqlog(qmul(q, conj(qp)));
@@ -591,7 +637,7 @@ template <class R, int T> struct Solver {
       J[1][0] -= R(0.5) * th.z; J[2][0] += R(0.5) * th.y;
       J[0][1] += R(0.5) * th.z; J[2][1] -= R(0.5) * th.x;
       J[0][2] -= R(0.5) * th.y; J[1][2] += R(0.5) * th.x;
-      const R *iw = S + L.IW + 6 * bi;   // xx, yy, zz, xy, xz, yz
+      const SV iw = S + (L.IW + kSIW * bi);   // xx, yy, zz, xy, xz, yz
       R Iw[3][3] = {{iw[0], iw[3], iw[4]}, {iw[3], iw[1], iw[5]}, {iw[4], iw[5], iw[2]}};
       R It[3], N[3][3];
 #pragma unroll
@@ -614,9 +660,9 @@ template <class R, int T> struct Solver {
       const int j = ldg(m->csrJoint[adj]);
       JointGeo e;
       evalJoint(j, e);
-      const bool parent = ldg(m->ja[j]) == bi;
+      const bool parent = e.a == bi;
       const R s = parent ? R(1) : R(-1);
-      const R *lam = S + L.JL + 7 * j, *pen = S + L.JP + 7 * j, *c0 = S + L.JC0 + 7 * j;
+      const SV lam = S + (L.JL + 7 * j), pen = S + (L.JP + 7 * j), c0 = S + (L.JC0 + 7 * j);
       const V3<R> r = parent ? e.ra : e.rb;
       R f3[3];
 #pragma unroll
@@ -639,7 +685,7 @@ template <class R, int T> struct Solver {
       }
       // Every remaining row acts along the hinge axis: J = (0, -s axis).
       R stiff = R(0), force = R(0);
-      if (ldg(m->limited[j])) {
+      if (e.limited) {
         R c5 = e.C[5] - alpha * rmin(c0[5], R(0));
         R f5 = rmin(lam[5] + pen[5] * c5, R(0));
         if (f5 < R(0)) { stiff += pen[5]; force += f5; }
@@ -672,11 +718,11 @@ template <class R, int T> struct Solver {
     }
     // Contacts touching bi, in list order.
     const int nGround = I[iGround];
-    const R *Rb = rot(bi);
+    const SV Rb = rot(bi);
     auto touch = [&](int ci) {
       const int meta = cmeta(ci);
       const int body = metaBody(meta), other = metaOther(meta);
-      const R *c = contact(ci);
+      const SV c = contact(ci);
       V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
       if (other < 0) {
         V3<R> ra = matVec(Rb, local);
@@ -690,7 +736,7 @@ template <class R, int T> struct Solver {
           geometric(H, ra, f);
         }
       } else {
-        const R *bs = S + L.CB + 9 * (ci - nGround);
+        const SV bs = S + (L.CB + 9 * (ci - nGround));
         V3<R> t1{bs[0], bs[1], bs[2]}, t2{bs[3], bs[4], bs[5]}, nn{bs[6], bs[7], bs[8]};
         V3<R> ra = matVec(rot(body), local), rb = matVec(rot(other), V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]});
         V3<R> delta = ld3(L.X + 3 * body) + ra - ld3(L.X + 3 * other) - rb;
@@ -737,7 +783,7 @@ template <class R, int T> struct Solver {
 
   // Contact gap C in the contact basis, C.z shifted by -alpha c0 (kernel.cuh:805-827).
   __device__ __forceinline__ V3<R> contactGap(int ci, int nGround) const {
-    const R *c = contact(ci);
+    const SV c = contact(ci);
     const int meta = cmeta(ci);
     const int body = metaBody(meta), other = metaOther(meta);
     V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
@@ -746,7 +792,7 @@ template <class R, int T> struct Solver {
     if (other < 0) {
       C = ld3(L.X + 3 * body) + ra - V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]};
     } else {
-      const R *bs = S + L.CB + 9 * (ci - nGround);
+      const SV bs = S + (L.CB + 9 * (ci - nGround));
       V3<R> rb = matVec(rot(other), V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]});
       V3<R> delta = ld3(L.X + 3 * body) + ra - ld3(L.X + 3 * other) - rb;
       C = {dot(delta, V3<R>{bs[0], bs[1], bs[2]}), dot(delta, V3<R>{bs[3], bs[4], bs[5]}),
@@ -783,8 +829,7 @@ template <class R, int T> struct Solver {
       S[L.JA0 + j] = e.angle;
       S[L.JLF + j] *= ag;
       S[L.JPF + j] = rclamp(S[L.JPF + j] * gamma, R(1), R(1e7));
-      const int a = ldg(m->ja[j]), b = ldg(m->jb[j]);
-      S[L.JV0 + j] = dot(omega(b) - omega(a), e.axis);
+      S[L.JV0 + j] = dot(omega(e.b) - omega(e.a), e.axis);
 #pragma unroll
       for (int k = 0; k < 7; ++k) {
         S[L.JL + 7 * j + k] *= ag;
@@ -794,19 +839,25 @@ template <class R, int T> struct Solver {
     }
     team.sync();
     // Predictor (kernel.cuh:965-976), one lane per body.  The predicted pose
-    // takes over the velocity slots of the body.
-    for (int b = team.lane; b < nb; b += T) {
-      V3<R> x = ld3(L.X + 3 * b);
-      Q4<R> q = ld4(L.Q + 4 * b);
-      st3(L.X0 + 3 * b, x);
-      st4(L.Q0 + 4 * b, q);
+    // takes over the velocity slots of the body; x0 and q0 stay in registers
+    // until velocity recovery, which uses the same lane for the same body.
+    V3<R> x0r[kPerLane];
+    Q4<R> q0r[kPerLane];
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k) {
+      const int b = team.lane + k * T;
+      if (b >= nb) continue;
+      const V3<R> x = ld3(L.X + 3 * b);
+      const Q4<R> q = quat(b);
+      x0r[k] = x;
+      q0r[k] = q;
       const R mass = ldg(m->mass[b]);
       if (mass == R(0)) continue;
       V3<R> in = mv3(m->inertia[b]);
       // World inertia R diag(I) R^T at q0 (kept for the whole substep).
-      const R *Rm = rot(b);
+      const SV Rm = rot(b);
       V3<R> ex{Rm[0], Rm[3], Rm[6]}, ey{Rm[1], Rm[4], Rm[7]}, ez{Rm[2], Rm[5], Rm[8]};
-      R *iw = S + L.IW + 6 * b;
+      SV iw = S + (L.IW + kSIW * b);
       iw[0] = in.x * ex.x * ex.x + in.y * ey.x * ey.x + in.z * ez.x * ez.x;
       iw[1] = in.x * ex.y * ex.y + in.y * ey.y * ey.y + in.z * ez.y * ez.y;
       iw[2] = in.x * ex.z * ex.z + in.y * ey.z * ey.z + in.z * ez.z * ez.z;
@@ -817,13 +868,13 @@ template <class R, int T> struct Solver {
       V3<R> grav{m->gravity[0], m->gravity[1], m->gravity[2]};
       V3<R> xp = x + v * h + (grav + bodyForce(b) * (R(1) / mass)) * (h * h);
       // Gyroscopic predictor: w + h I^-1 (-(w x I w)), body frame.
-      V3<R> wl{Rm[0] * w.x + Rm[3] * w.y + Rm[6] * w.z, Rm[1] * w.x + Rm[4] * w.y + Rm[7] * w.z,
-               Rm[2] * w.x + Rm[5] * w.y + Rm[8] * w.z};
+      V3<R> wl{ex.x * w.x + ex.y * w.y + ex.z * w.z, ey.x * w.x + ey.y * w.y + ey.z * w.z,
+               ez.x * w.x + ez.y * w.y + ez.z * w.z};
       V3<R> Iwl{in.x * wl.x, in.y * wl.y, in.z * wl.z};
       V3<R> tl = -cross(wl, Iwl);
       V3<R> wp = w + matVec(Rm, V3<R>{tl.x / in.x, tl.y / in.y, tl.z / in.z}) * h;
       Q4<R> qp = qmul(fqexp(wp * h), q);
-      R *xqp = S + L.XQP + 7 * b;
+      SV xqp = S + (L.XQP + 7 * b);
       xqp[0] = xp.x; xqp[1] = xp.y; xqp[2] = xp.z;
       xqp[3] = qp.w; xqp[4] = qp.x; xqp[5] = qp.y; xqp[6] = qp.z;
       setPose(b, xp, qp);
@@ -854,9 +905,8 @@ template <class R, int T> struct Solver {
       for (int j = team.lane; j < nj; j += T) {
         JointGeo e;
         evalJoint(j, e);
-        R *lam = S + L.JL + 7 * j, *pen = S + L.JP + 7 * j;
-        const R *c0 = S + L.JC0 + 7 * j;
-        const int rows = ldg(m->limited[j]) ? 7 : 5;
+        const SV lam = S + (L.JL + 7 * j), pen = S + (L.JP + 7 * j), c0 = S + (L.JC0 + 7 * j);
+        const int rows = e.limited ? 7 : 5;
         for (int k = 0; k < rows; ++k) {
           R c = e.C[k] - alpha * (k < 5 ? c0[k] : rmin(c0[k], R(0)));
           R f = lam[k] + pen[k] * c;
@@ -881,7 +931,7 @@ template <class R, int T> struct Solver {
       // Contact multipliers, stick flags and penalties (kernel.cuh:1029-1052).
       const int n = I[iCount], nGround = I[iGround];
       for (int ci = team.lane; ci < n; ci += T) {
-        R *c = contact(ci);
+        const SV c = contact(ci);
         const V3<R> C = contactGap(ci, nGround);
         V3<R> f = coneForce(C, c);
         R tx = c[cLambda] + c[cPenalty] * C.x, ty = c[cLambda + 1] + c[cPenalty + 1] * C.y;
@@ -909,12 +959,14 @@ template <class R, int T> struct Solver {
     // Velocity recovery (kernel.cuh:1064-1073); the velocities return to the
     // XQP slots.
     bool bad = false;
-    for (int b = team.lane; b < nb; b += T) {
-      if (!(ldg(m->mass[b]) > R(0))) continue;
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k) {
+      const int b = team.lane + k * T;
+      if (b >= nb || !(ldg(m->mass[b]) > R(0))) continue;
       V3<R> x = ld3(L.X + 3 * b);
-      V3<R> v = (x - ld3(L.X0 + 3 * b)) * (R(1) / h);
-      V3<R> w = fqlog(qmul(ld4(L.Q + 4 * b), conj(ld4(L.Q0 + 4 * b)))) * (R(1) / h);
-      R *vw = S + L.XQP + 7 * b;
+      V3<R> v = (x - x0r[k]) * (R(1) / h);
+      V3<R> w = fqlog(qmul(quat(b), conj(q0r[k]))) * (R(1) / h);
+      SV vw = S + (L.XQP + 7 * b);
       vw[0] = v.x; vw[1] = v.y; vw[2] = v.z; vw[3] = w.x; vw[4] = w.y; vw[5] = w.z;
       if (!isfinite(dot(x, x) + dot(v, v) + dot(w, w))) bad = true;
     }
@@ -985,9 +1037,11 @@ __global__ void __launch_bounds__(32) advanceKernel(const DevModel<R> *__restric
   const int team = threadIdx.x / T;
   const int env = blockIdx.x * teams + team;
   if (env >= count) return;
-  R *S = reinterpret_cast<R *>(smemRaw) + size_t(team) * L.size;
+  // Teams are interleaved word by word: team t owns words t, t + teams, ...
+  R *teamBase = reinterpret_cast<R *>(smemRaw) + team;
   R *rec = records + size_t(env) * recordStride;
-  Solver<R, T> s(model, points, S, rec, L);
+  Solver<R, T> s(model, points, teamBase, rec, L);
+  const typename Solver<R, T>::SV S = s.S;
   const int nj = model->nj;
   const int lane = s.team.lane;
   const R *forces = static_cast<const R *>(args.forces) + 3 * size_t(env);
