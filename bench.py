@@ -266,13 +266,14 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
     from duck_gym_b200 import CudaBatch, fp32_peak_tflops
+    from duck_gym_b200.sharding import max_over_ranks, rank_seed, weak_shard
 
     with tempfile.TemporaryDirectory() as d:
         model, meta = make_model(d)
         kp, limit = meta["kp"], meta["torque_limit"]
-        envs = args.envs
+        envs = weak_shard(args.envs, rank, world).count   # weak scaling: envs per GPU fixed
         batch = CudaBatch(model, envs, DT, ITERATIONS, local)
-        target_host = fixed_targets(meta, envs, 1000 * rank)
+        target_host = fixed_targets(meta, envs, rank_seed(0, rank))
         target = torch.from_numpy(target_host).to(device)
         forces = torch.zeros(envs, 3, device=device)
         for _ in range(SETTLE):
@@ -307,10 +308,7 @@ def main():
         launches = batch.launches - launches0
         kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
         device_s = sum(kernel_ms) / 1e3
-        t = torch.tensor([device_s], device=device, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        slowest = float(t.item())
+        slowest = max_over_ranks(device_s, device)
         total_steps = envs * SUBSTEPS * args.steps * world
         value = total_steps / slowest
 
@@ -332,10 +330,7 @@ def main():
             host_out.copy_(diag, non_blocking=True)
         e1.record(stream)
         barrier()
-        e2e_s = torch.tensor([e0.elapsed_time(e1) / 1e3], device=device, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
-        e2e_value = envs * SUBSTEPS * e2e_steps * world / float(e2e_s.item())
+        e2e_value = envs * SUBSTEPS * e2e_steps * world / max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
         failed_fraction = float((host_out[:, 5] > 0).float().mean())
 
         line = None
