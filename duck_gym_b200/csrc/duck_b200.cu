@@ -7,6 +7,7 @@
 // src/cuda/extension.cu:203-205) and launches on the caller's stream.
 #include "../../include/duck_b200.h"
 #include "aux_kernels.cuh"
+#include "env_kernels.cuh"
 
 #include <cstdlib>
 #include <cstring>
@@ -523,6 +524,132 @@ int duck_batch_reference_static(duck_batch *b, const void *target, const void *f
     check(cudaMemcpy(bodies, dBodies, 13 * b->nb * real, cudaMemcpyDeviceToHost), "copy bodies");
     if (b->nj) check(cudaMemcpy(joints, dJoints, 2 * b->nj * real, cudaMemcpyDeviceToHost), "copy joints");
     check(cudaMemcpy(diag, dDiag, 6 * real, cudaMemcpyDeviceToHost), "copy diag");
+  });
+}
+
+}  // extern "C"
+
+namespace {
+EnvKernelParams envParams(const duck_batch *b, const duck_env_params *p) {
+  require(p != nullptr, "Invalid arguments");
+  require(p->task == 0 || p->task == 1, "Unknown task");
+  require(p->control_dt > 0 && p->tracking_sigma > 0 && p->gait_period > 0 && p->max_episode_length > 0,
+          "Invalid environment parameters");
+  EnvKernelParams k{};
+  k.task = p->task;
+  k.filter = p->filter ? 1 : 0;
+  k.maxEpisode = p->max_episode_length;
+  k.nj = b->nj;
+  k.obsDim = 10 + 3 * b->nj + (p->task == 1 ? 6 : 0) + (k.filter ? 2 : 0);
+  k.rootHeight = p->root_height;
+  k.tilt = float(p->tilt);
+  k.controlDt = p->control_dt;
+  k.velocityAlpha = p->velocity_alpha;
+  k.trackingWeight = p->tracking_weight;
+  k.headingWeight = p->heading_weight;
+  k.sigma2 = p->tracking_sigma * p->tracking_sigma;
+  k.phaseRate = 2 * 3.14159265358979323846 / p->gait_period;
+  for (int i = 0; i < 4; ++i) k.iquat[i] = p->iquat[i];
+  return k;
+}
+}  // namespace
+
+extern "C" {
+
+int duck_env_obs_dim(const duck_batch *b, const duck_env_params *p) {
+  if (!b || !p) return -1;
+  return 10 + 3 * b->nj + (p->task == 1 ? 6 : 0) + (p->filter ? 2 : 0);
+}
+
+int duck_env_targets(duck_batch *b, const void *actions, double scale, const void *home, const void *lower,
+                     const void *upper, void *a_out, void *target_out, duck_stream stream) {
+  return guarded([&] {
+    require(b && actions && home && lower && upper && a_out && target_out, "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int items = b->n * b->nj;
+    if (items == 0) return;
+    if (b->fp64)
+      envTargetsKernel<double><<<blocksFor(items, 256), 256, 0, s>>>(
+          b->n, b->nj, static_cast<const double *>(actions), scale, static_cast<const double *>(home), static_cast<const double *>(lower),
+          static_cast<const double *>(upper), static_cast<double *>(a_out), static_cast<double *>(target_out));
+    else
+      envTargetsKernel<float><<<blocksFor(items, 256), 256, 0, s>>>(
+          b->n, b->nj, static_cast<const float *>(actions), float(scale), static_cast<const float *>(home), static_cast<const float *>(lower),
+          static_cast<const float *>(upper), static_cast<float *>(a_out), static_cast<float *>(target_out));
+    ++b->launches;
+    check(cudaGetLastError(), "env targets");
+  });
+}
+
+int duck_env_post_step(duck_batch *b, const duck_env_params *params, const void *home, const void *a,
+                       void *prev_actions, int64_t *episode_length, float *returns, const void *commands,
+                       void *filtered, float *obs, float *reward, uint8_t *failed, uint8_t *timeout,
+                       uint8_t *done, void *diag, float *tracking, duck_stream stream) {
+  return guarded([&] {
+    require(b && home && a && prev_actions && episode_length && returns && commands && filtered && obs && reward &&
+                failed && timeout && done,
+            "Invalid arguments");
+    const EnvKernelParams k = envParams(b, params);
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    begin(b, s);
+    auto run = [&](auto zero) {
+      using R = decltype(zero);
+      envPostStepKernel<R><<<blocksFor(b->n, 128), 128, 0, s>>>(
+          static_cast<const DevModel<R> *>(b->devModel), static_cast<const R *>(b->records), b->recordStride, b->n,
+          k, static_cast<const R *>(home), static_cast<const R *>(a), static_cast<R *>(prev_actions),
+          reinterpret_cast<long long *>(episode_length), returns, static_cast<const R *>(commands),
+          static_cast<R *>(filtered), obs, reward, reinterpret_cast<bool *>(failed),
+          reinterpret_cast<bool *>(timeout), reinterpret_cast<bool *>(done), static_cast<R *>(diag), tracking);
+    };
+    if (b->fp64) run(0.0); else run(0.0f);
+    ++b->launches;
+    finish(b, s);
+  });
+}
+
+int duck_env_observe(duck_batch *b, const duck_env_params *params, const void *home, const void *actions,
+                     const int64_t *episode_length, const void *commands, const void *filtered, float *obs,
+                     duck_stream stream) {
+  return guarded([&] {
+    require(b && home && actions && episode_length && commands && filtered && obs, "Invalid arguments");
+    const EnvKernelParams k = envParams(b, params);
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    begin(b, s);
+    auto run = [&](auto zero) {
+      using R = decltype(zero);
+      envObserveKernel<R><<<blocksFor(b->n, 128), 128, 0, s>>>(
+          static_cast<const DevModel<R> *>(b->devModel), static_cast<const R *>(b->records), b->recordStride, b->n,
+          k, static_cast<const R *>(home), static_cast<const R *>(actions),
+          reinterpret_cast<const long long *>(episode_length), static_cast<const R *>(commands),
+          static_cast<const R *>(filtered), obs);
+    };
+    if (b->fp64) run(0.0); else run(0.0f);
+    ++b->launches;
+    finish(b, s);
+  });
+}
+
+int duck_env_reset_buffers(duck_batch *b, const uint8_t *mask, void *prev_actions, void *forces,
+                           int64_t *episode_length, float *returns, void *filtered, void *commands,
+                           const void *new_commands, duck_stream stream) {
+  return guarded([&] {
+    require(b && mask && prev_actions && forces && episode_length && returns && filtered && commands,
+            "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    auto run = [&](auto zero) {
+      using R = decltype(zero);
+      envResetBuffersKernel<R><<<blocksFor(b->n, 128), 128, 0, s>>>(
+          b->n, b->nj, reinterpret_cast<const bool *>(mask), static_cast<R *>(prev_actions), static_cast<R *>(forces),
+          reinterpret_cast<long long *>(episode_length), returns, static_cast<R *>(filtered),
+          static_cast<R *>(commands), static_cast<const R *>(new_commands));
+    };
+    if (b->fp64) run(0.0); else run(0.0f);
+    ++b->launches;
+    check(cudaGetLastError(), "env reset buffers");
   });
 }
 

@@ -69,11 +69,17 @@ def library():
         lib.duck_batch_launches.argtypes = [P]
         lib.duck_batch_launches.restype = ctypes.c_int64
         lib.duck_fp32_peak.argtypes = [I, I, ctypes.POINTER(D), P]
+        lib.duck_env_obs_dim.argtypes = [P, P]
+        lib.duck_env_targets.argtypes = [P, P, D, P, P, P, P, P, P]
+        lib.duck_env_post_step.argtypes = [P] * 17
+        lib.duck_env_observe.argtypes = [P] * 9
+        lib.duck_env_reset_buffers.argtypes = [P] * 10
         for name in ("duck_batch_create", "duck_batch_info", "duck_batch_reset", "duck_batch_step",
                      "duck_batch_step_motor", "duck_batch_state", "duck_batch_contact_forces",
                      "duck_batch_self_contact_stats", "duck_batch_contact_counts",
                      "duck_batch_generalized_loads", "duck_batch_reference", "duck_batch_export",
-                     "duck_batch_import", "duck_batch_contact_keys", "duck_fp32_peak"):
+                     "duck_batch_import", "duck_batch_contact_keys", "duck_fp32_peak", "duck_env_obs_dim",
+                     "duck_env_targets", "duck_env_post_step", "duck_env_observe", "duck_env_reset_buffers"):
             getattr(lib, name).restype = I
         _lib = lib
     return _lib

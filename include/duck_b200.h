@@ -137,6 +137,55 @@ int duck_batch_import(duck_batch *batch, int first, int count, const void *recor
 int duck_batch_contact_keys(duck_batch *batch, int env, int32_t *keys, int capacity, int *count,
                             duck_stream stream);
 
+/* Tensor environment (the reference's python/duck_gym/tensor_env.py step math)
+ * fused into three kernels that read the batch's physics state directly.
+ * Buffers are device arrays of the batch dtype (Real) unless noted; episode
+ * lengths are int64, returns, observations and rewards float32, masks bool.
+ * task: 0 standing, 1 locomotion; filter: velocity filter on (locomotion);
+ * tilt: -cos(0.5) as the env computes it on its device. */
+typedef struct duck_env_params {
+  int task, filter, max_episode_length;
+  double root_height, tilt, control_dt, velocity_alpha, tracking_weight, heading_weight, tracking_sigma,
+      gait_period;
+  double iquat[4]; /* conjugated root principal-frame quaternion (w, x, y, z) */
+} duck_env_params;
+
+/* Observation width of the environment described by params (52, 58 or 60 for
+ * the 14-joint biped). */
+int duck_env_obs_dim(const duck_batch *batch, const duck_env_params *params);
+
+/* tensor_env.py:280-283: a = clamp(actions, -1, 1), target = clamp(home +
+ * scale a, lower, upper).  actions, a_out, target_out [E,J]; home, lower,
+ * upper [J]. */
+int duck_env_targets(duck_batch *batch, const void *actions, double scale, const void *home,
+                     const void *lower, const void *upper, void *a_out, void *target_out,
+                     duck_stream stream);
+
+/* tensor_env.py:291-361 after the physics step: projected gravity and body
+ * velocities, termination (failed), reward, time-outs, done, episode
+ * lengths (+1), returns (+reward), prev_actions := a, velocity filter, and the
+ * terminal observation obs [E,D].  Optional outputs (NULL to skip): diag
+ * [E,6] as duck_batch_state writes it, and tracking [E,4] float32 with the
+ * per-env terms of the locomotion log (|v_xy - command|, v_xy . command,
+ * sqrt of the reward's velocity error, |heading angle|). */
+int duck_env_post_step(duck_batch *batch, const duck_env_params *params, const void *home,
+                       const void *a, void *prev_actions, int64_t *episode_length, float *returns,
+                       const void *commands, void *filtered, float *obs, float *reward,
+                       uint8_t *failed, uint8_t *timeout, uint8_t *done, void *diag, float *tracking,
+                       duck_stream stream);
+
+/* tensor_env.py:238-261: observations [E,D] of the current state. */
+int duck_env_observe(duck_batch *batch, const duck_env_params *params, const void *home,
+                     const void *actions, const int64_t *episode_length, const void *commands,
+                     const void *filtered, float *obs, duck_stream stream);
+
+/* tensor_env.py:197-219: for masked environments zero prev_actions [E,J],
+ * forces [E,3], episode_length, returns and filtered [E,2], and copy
+ * new_commands [E,2] into commands (new_commands may be NULL). */
+int duck_env_reset_buffers(duck_batch *batch, const uint8_t *mask, void *prev_actions, void *forces,
+                           int64_t *episode_length, float *returns, void *filtered, void *commands,
+                           const void *new_commands, duck_stream stream);
+
 /* No reference counterpart.  Number of kernel launches issued by this batch
  * since creation (for launch accounting in benchmarks). */
 int64_t duck_batch_launches(const duck_batch *batch);

@@ -28,6 +28,28 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, name), name
 
 
+def declared_arity():
+    """Parameter count of every function declared in the header."""
+    text = (ROOT / "include" / "duck_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(duck_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        params = params.strip()
+        out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_python_binding_matches_declared_signatures():
+    from duck_gym_b200 import cuda_batch
+
+    lib = cuda_batch.library()
+    arity = declared_arity()
+    bound = [n for n in arity if getattr(lib, n).argtypes is not None]
+    assert len(bound) >= 20
+    for name in bound:
+        assert len(getattr(lib, name).argtypes) == arity[name], name
+
+
 def test_library_has_no_torch_dependency():
     from duck_gym_b200 import build
 

@@ -1,0 +1,35 @@
+"""CPU: host-side checks of duck_gym_b200.TensorEnv (argument handling of the
+reference's constructor, tensor_env.py:59-176), raised before any device work."""
+
+import pytest
+
+from duck_gym_b200.tensor_env import TensorEnv
+
+
+@pytest.mark.parametrize("kwargs,error", [
+    (dict(substeps=0), ValueError),
+    (dict(episode_seconds=0), ValueError),
+    (dict(action_scale=0), ValueError),
+    (dict(backend="tpu"), ValueError),
+    (dict(backend="cpu"), ValueError),
+    (dict(gait=True), NotImplementedError),
+    (dict(foot_clearance=True), NotImplementedError),
+    (dict(load_transfer=True), NotImplementedError),
+])
+def test_constructor_rejects(biped_dir, kwargs, error):
+    with pytest.raises(error):
+        TensorEnv(biped_dir, **kwargs)
+
+
+def test_params_layout_matches_header():
+    import ctypes
+    import re
+    from pathlib import Path
+
+    from duck_gym_b200.tensor_env import EnvParams
+
+    header = (Path(__file__).resolve().parents[1] / "include" / "duck_b200.h").read_text()
+    body = re.search(r"typedef struct duck_env_params \{(.*?)\} duck_env_params;", header, re.S).group(1)
+    names = re.findall(r"\b([a-z_]+)(?:\[4\])?\s*[,;]", re.sub(r"/\*.*?\*/", "", body, flags=re.S))
+    assert [n for n, _ in EnvParams._fields_] == names
+    assert ctypes.sizeof(EnvParams) == 4 * 3 + 4 + 8 * 8 + 8 * 4
