@@ -287,6 +287,73 @@ def generate(seed: int = 0, self_contacts: bool = False):
     return text, meta
 
 
+# Synthetic stand-in for the pinned BAM XL330/m6 parameter file (the reference
+# loads it from the third-party ``bam`` package, bam/params/xl330/m6.json at
+# commit 62bd8ce, which is not available here).  The keys are the ones the
+# reference actuator reads (python/duck_gym/actuator.py:46-73).  The values are
+# chosen, not fitted: with vin 7 V and kp_fw 993 the servo behaves as the BAM
+# motor model of the self-contact configuration -- proportional gain
+# kt vin kp_fw g / R = 4.0 N m/rad (g = 4096 / (2 pi) / (256 * 885) counts per
+# radian over the firmware scale), back-EMF damping kt^2 / R = 0.1 N m s/rad,
+# torque limit 0.5 N m -- plus load- and speed-dependent dry friction.
+BAM_PARAMETERS = dict(
+    kt=0.5, R=2.5, friction_base=0.004, friction_stribeck=0.003, load_friction_external=0.02,
+    load_friction_motor=0.015, load_friction_external_stribeck=0.01, load_friction_motor_stribeck=0.008,
+    load_friction_external_quad=0.04, load_friction_motor_quad=0.03, dtheta_stribeck=0.2, alpha=1.4,
+    friction_viscous=0.006,
+)
+BAM_SUPPLY = dict(kp_fw=993.0, vin=7.0, vin_drop_gain=0.1, vin_min=6.0, force_limit=0.5)
+FOOT_JOINTS = ("left_ankle", "right_ankle")
+
+
+def bam_config(text: str, meta: dict, physics_dt: float = 0.005, decimation: int = 4,
+               delay_lag_steps=(1, 3), root_com_offset=(0.004, 0.0, -0.006)) -> dict:
+    """The ``config.json`` of a BAM bundle for a generated biped, with the keys
+    the reference ``BamEnv`` reads (python/duck_gym/bam_env.py:33-133, written
+    by scripts/prepare_official_model.py:109-145 from MuJoCo there): foot
+    bodies with their collision corners and sole sites in body coordinates,
+    HOME as ``default_qpos[7:]``, and the synthetic servo parameters above."""
+    lines = text.splitlines()
+    n_bodies = int(lines[0].split()[2])
+    n_joints = int(lines[0].split()[3])
+    shape_rows = [line.split() for line in lines[2 + n_bodies + n_joints:2 + n_bodies + n_joints + int(lines[0].split()[4])]]
+    feet = []
+    for joint in FOOT_JOINTS:
+        body = 2 + JOINT_NAMES.index(joint)
+        row = next(r for r in shape_rows if int(r[0]) == body)
+        hx, hy, hz = (float(v) for v in row[9:12])
+        cx, cy, cz = (float(v) for v in row[2:5])
+        corners = [[cx + sx * hx, cy + sy * hy, cz + sz * hz] for sx in (-1, 1) for sy in (-1, 1) for sz in (-1, 1)]
+        feet.append(dict(body=body, points=corners, site=[cx, cy, cz - hz]))
+    base = lines[3].split()
+    return dict(
+        scope="Synthetic biped bundle (duck_gym_b200.biped); BAM parameters are chosen stand-ins",
+        physics_dt=physics_dt,
+        decimation=decimation,
+        default_qpos=[float(v) for v in base[5:8]] + [float(v) for v in base[8:12]] + list(meta["home"]),
+        root_com_offset=list(root_com_offset),
+        root_principal_quat=list(meta["root_iquat"]),
+        feet=feet,
+        masses=[float(line.split()[1]) for line in lines[2:2 + n_bodies]],
+        joint_names=list(meta["joint_names"]),
+        parameters=dict(BAM_PARAMETERS),
+        delay_lag_steps=list(delay_lag_steps),
+        **BAM_SUPPLY,
+    )
+
+
+def write_bam(directory, seed: int = 0, self_contacts: bool = False, **kwargs):
+    """Write a BAM bundle (``model.duck`` + ``config.json`` + ``metadata.json``)
+    for the seeded biped; return the directory."""
+    directory = Path(directory)
+    directory.mkdir(parents=True, exist_ok=True)
+    text, meta = generate(seed, self_contacts)
+    (directory / "model.duck").write_text(text)
+    (directory / "metadata.json").write_text(json.dumps(meta, indent=2) + "\n")
+    (directory / "config.json").write_text(json.dumps(bam_config(text, meta, **kwargs), indent=2) + "\n")
+    return directory
+
+
 def write(directory, seed: int = 0, self_contacts: bool = False, name: str = "microduck.duck"):
     """Write ``<directory>/<name>`` and ``metadata.json``; return the model path."""
     directory = Path(directory)
