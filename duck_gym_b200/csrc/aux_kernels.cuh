@@ -138,44 +138,69 @@ __global__ void contactForcesKernel(const DevModel<R> *__restrict__ m, const R *
   }
 }
 
+// Self-contact statistics of one environment (kernel.cuh:481-498): ground
+// and self contact counts, active self contacts and the deepest self
+// penetration.
+template <class R> struct ContactStats {
+  R ground, self, active, depthMax;
+};
+template <class R>
+__device__ __forceinline__ ContactStats<R> envContactStats(const DevModel<R> *m, const R *rec, bool self) {
+  const R *bodies = rec + kRecHeader;
+  const R *cs = recContacts(m, rec);
+  const int n = int(rec[1]);
+  ContactStats<R> st{R(0), R(0), R(0), R(0)};
+  for (int i = 0; i < n; ++i) {
+    const R *c = cs + kRecContact * i;
+    const int body = int(c[0]), other = int(c[3]);
+    if (other < 0) { st.ground += R(1); continue; }
+    st.self += R(1);
+    if (!self) continue;
+    V3<R> ra = rotate(gq4(bodies + kRecBody * body + 3), V3<R>{c[6], c[7], c[8]});
+    V3<R> rb = rotate(gq4(bodies + kRecBody * other + 3), V3<R>{c[12], c[13], c[14]});
+    V3<R> delta = gv3(bodies + kRecBody * body) + ra - gv3(bodies + kRecBody * other) - rb;
+    R gapN = dot(delta, V3<R>{c[21], c[22], c[23]});
+    R depth = rmax(R(0), -gapN);
+    if (c[28] < R(-1e-5) || depth > R(1e-6)) st.active += R(1);
+    st.depthMax = rmax(st.depthMax, depth);
+  }
+  return st;
+}
+
 // contactCounts / selfContactStats (kernel.cuh:481-498).
 template <class R>
 __global__ void contactStatsKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
                                    R *counts, R *selfStats) {
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= count) return;
-  const R *rec = records + size_t(e) * stride;
-  const R *bodies = rec + kRecHeader;
+  const ContactStats<R> st = envContactStats(m, records + size_t(e) * stride, selfStats != nullptr);
+  if (counts) { counts[2 * size_t(e)] = st.ground; counts[2 * size_t(e) + 1] = st.self; }
+  if (selfStats) { selfStats[2 * size_t(e)] = st.active; selfStats[2 * size_t(e) + 1] = st.depthMax; }
+}
+
+// Ground contact force on one body, summed in contact order as
+// contactForcesKernel does (kernel.cuh:467-480).
+template <class R>
+__device__ __forceinline__ V3<R> envGroundForce(const DevModel<R> *m, const R *rec, int body) {
   const R *cs = recContacts(m, rec);
   const int n = int(rec[1]);
-  R ground = R(0), self = R(0), active = R(0), depthMax = R(0);
+  V3<R> f{R(0), R(0), R(0)};
   for (int i = 0; i < n; ++i) {
     const R *c = cs + kRecContact * i;
-    const int body = int(c[0]), other = int(c[3]);
-    if (other < 0) { ground += R(1); continue; }
-    self += R(1);
-    if (!selfStats) continue;
-    V3<R> ra = rotate(gq4(bodies + kRecBody * body + 3), V3<R>{c[6], c[7], c[8]});
-    V3<R> rb = rotate(gq4(bodies + kRecBody * other + 3), V3<R>{c[12], c[13], c[14]});
-    V3<R> delta = gv3(bodies + kRecBody * body) + ra - gv3(bodies + kRecBody * other) - rb;
-    R gapN = dot(delta, V3<R>{c[21], c[22], c[23]});
-    R depth = rmax(R(0), -gapN);
-    if (c[28] < R(-1e-5) || depth > R(1e-6)) active += R(1);
-    depthMax = rmax(depthMax, depth);
+    if (int(c[0]) != body || int(c[3]) >= 0) continue;
+    V3<R> g = -recContactWorld(c, V3<R>{c[26], c[27], c[28]});
+    f.x += g.x; f.y += g.y; f.z += g.z;
   }
-  if (counts) { counts[2 * size_t(e)] = ground; counts[2 * size_t(e) + 1] = self; }
-  if (selfStats) { selfStats[2 * size_t(e)] = active; selfStats[2 * size_t(e) + 1] = depthMax; }
+  return f;
 }
 
 // BasicState::generalizedLoads (kernel.cuh:504-554): RNEA at zero joint
-// acceleration, one thread per environment.
+// acceleration for one environment; out [J,3] = (bias, contact + limit,
+// applied actuator) per hinge.
 template <class R>
-__global__ void generalizedLoadsKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
-                                       const R *offset, R *out) {
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= count) return;
+__device__ __noinline__ void envGeneralizedLoads(const DevModel<R> *__restrict__ m, const R *rec, V3<R> off,
+                                                 R *o) {
   const int nb = m->nb, nj = m->nj;
-  const R *rec = records + size_t(e) * stride;
   const R *bodies = rec + kRecHeader;
   const R *joints = bodies + kRecBody * nb;
   V3<R> acc[kMaxBodies], alpha[kMaxBodies], force[kMaxBodies], moment[kMaxBodies], contact[kMaxBodies],
@@ -185,8 +210,7 @@ __global__ void generalizedLoadsKernel(const DevModel<R> *__restrict__ m, const 
   auto X = [&](int b) { return gv3(bodies + kRecBody * b); };
   auto Q = [&](int b) { return gq4(bodies + kRecBody * b + 3); };
   auto W = [&](int b) { return gv3(bodies + kRecBody * b + 10); };
-  const R *off = offset + 3 * size_t(e);
-  acc[1] = cross(W(1), cross(W(1), rotate(Q(1), V3<R>{off[0], off[1], off[2]})));
+  acc[1] = cross(W(1), cross(W(1), rotate(Q(1), off)));
   for (int j = 0; j < nj; ++j) {
     const int a = __ldg(&m->ja[j]), b = __ldg(&m->jb[j]);
     V3<R> axis = rotate(Q(a), mvec(m->axisA[j])), ra = rotate(Q(a), mvec(m->ra[j])), rb = rotate(Q(b), mvec(m->rb[j]));
@@ -219,7 +243,6 @@ __global__ void generalizedLoadsKernel(const DevModel<R> *__restrict__ m, const 
       contactMoment[other] = contactMoment[other] + cross(rotate(Q(other), V3<R>{c[12], c[13], c[14]}), -f);
     }
   }
-  R *o = out + size_t(e) * nj * 3;
   for (int k = nj - 1; k >= 0; --k) {
     const int a = __ldg(&m->ja[k]), b = __ldg(&m->jb[k]);
     const R *jr = joints + kRecJoint * k;
@@ -237,6 +260,16 @@ __global__ void generalizedLoadsKernel(const DevModel<R> *__restrict__ m, const 
     contactMoment[a] = contactMoment[a] + (contactMoment[b] + cross(shift, contact[b]));
     contact[a] = contact[a] + contact[b];
   }
+}
+
+// BasicState::generalizedLoads (kernel.cuh:504-554), one thread per environment.
+template <class R>
+__global__ void generalizedLoadsKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
+                                       const R *offset, R *out) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= count) return;
+  const R *off = offset + 3 * size_t(e);
+  envGeneralizedLoads(m, records + size_t(e) * stride, V3<R>{off[0], off[1], off[2]}, out + size_t(e) * m->nj * 3);
 }
 
 // Validation of the generalized-load offsets happens on the device: a

@@ -7,7 +7,7 @@
 // src/cuda/extension.cu:203-205) and launches on the caller's stream.
 #include "../../include/duck_b200.h"
 #include "aux_kernels.cuh"
-#include "env_kernels.cuh"
+#include "bam_kernels.cuh"
 
 #include <cstdlib>
 #include <cstring>
@@ -71,10 +71,21 @@ struct DeviceGuard {
   ~DeviceGuard() { cudaSetDevice(previous); }
 };
 
-void begin(duck_batch *b, cudaStream_t s) { check(cudaStreamWaitEvent(s, b->ready, 0), "cudaStreamWaitEvent"); }
+// Calls are ordered across streams by the batch's private event.  While the
+// stream is being captured into a CUDA graph the event is left alone: the
+// graph's own edges order the captured work, and an event recorded outside the
+// capture cannot be waited on inside it.
+bool capturing(cudaStream_t s) {
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  check(cudaStreamIsCapturing(s, &status), "cudaStreamIsCapturing");
+  return status != cudaStreamCaptureStatusNone;
+}
+void begin(duck_batch *b, cudaStream_t s) {
+  if (!capturing(s)) check(cudaStreamWaitEvent(s, b->ready, 0), "cudaStreamWaitEvent");
+}
 void finish(duck_batch *b, cudaStream_t s) {
   check(cudaGetLastError(), "kernel launch");
-  check(cudaEventRecord(b->ready, s), "cudaEventRecord");
+  if (!capturing(s)) check(cudaEventRecord(b->ready, s), "cudaEventRecord");
 }
 int blocksFor(long long threads, int per) { return int((threads + per - 1) / per); }
 
@@ -650,6 +661,223 @@ int duck_env_reset_buffers(duck_batch *b, const uint8_t *mask, void *prev_action
     if (b->fp64) run(0.0); else run(0.0f);
     ++b->launches;
     check(cudaGetLastError(), "env reset buffers");
+  });
+}
+
+}  // extern "C"
+
+namespace {
+BamKernelParams bamParams(const duck_batch *b, const duck_bam_params *p) {
+  require(p != nullptr, "Invalid arguments");
+  require(b->nj > 0 && b->nj <= 32, "The BAM environment needs 1..32 joints");
+  require(p->lag >= 0 && p->decimation >= 1 && p->max_episode_length > 0 && p->dt > 0 && p->step_dt > 0,
+          "Invalid BAM control settings");
+  require(p->foot_body[0] > 0 && p->foot_body[0] < b->nb && p->foot_body[1] > 0 && p->foot_body[1] < b->nb,
+          "Foot body index out of range");
+  require(p->vin_min > 0 && p->R > 0 && p->dtheta_stribeck > 0 && p->force_limit >= 0, "Invalid servo parameters");
+  int heads = 0;
+  for (int j = 0; j < b->nj; ++j) heads += (p->head_mask >> j) & 1;
+  require(heads == 4, "The walking reward needs exactly four head joints");
+  BamKernelParams k{};
+  k.nj = b->nj;
+  k.lag = p->lag;
+  k.maxEpisode = p->max_episode_length;
+  k.sourceIteration = p->source_iteration;
+  k.neutralHead = p->neutral_head;
+  k.headingHold = p->heading_hold;
+  k.reward = p->reward_enabled;
+  k.headMask = int(p->head_mask);
+  k.extras = (p->head_stability ? xHeadStability : 0) | (p->mean_velocity ? xMeanVelocity : 0) |
+             (p->heading_reward ? xHeading : 0);
+  k.overrideMask = int(p->override_mask);
+  k.criticDim = 34 + 3 * b->nj + (p->mean_velocity ? 3 : 0) + (p->heading_reward ? 1 : 0);
+  k.footBody[0] = p->foot_body[0];
+  k.footBody[1] = p->foot_body[1];
+  k.dt = p->dt; k.stepDt = p->step_dt; k.kpFw = p->kp_fw; k.vin = p->vin; k.vinDrop = p->vin_drop_gain;
+  k.vinMin = p->vin_min; k.forceLimit = p->force_limit;
+  k.kt = p->kt; k.res = p->R; k.fBase = p->friction_base; k.fStribeck = p->friction_stribeck;
+  k.lfe = p->load_friction_external; k.lfm = p->load_friction_motor; k.lfes = p->load_friction_external_stribeck;
+  k.lfms = p->load_friction_motor_stribeck; k.lfeq = p->load_friction_external_quad;
+  k.lfmq = p->load_friction_motor_quad; k.dthetaStribeck = p->dtheta_stribeck; k.alpha = p->alpha;
+  k.fViscous = p->friction_viscous;
+  for (int i = 0; i < 4; ++i) k.iquat[i] = p->root_iquat[i];
+  for (int f = 0; f < 2; ++f)
+    for (int i = 0; i < 3; ++i) k.site[f][i] = p->foot_site[f][i];
+  k.linVar = p->linear_variance; k.vertVar = p->vertical_variance; k.meanAlpha = p->mean_velocity_alpha;
+  k.meanVar = p->mean_velocity_variance; k.meanWeight = p->mean_velocity_weight;
+  k.headingWeight = p->heading_reward_weight; k.headingVar = p->heading_reward_variance;
+  k.headPosWeight = p->head_position_weight; k.headVelWeight = p->head_velocity_weight;
+  k.tiltLimit = p->tilt_limit;
+  for (int t = 0; t < 15; ++t) k.overrides[t] = p->overrides[t];
+  for (int j = 0; j < 32; ++j) {
+    k.stand[j] = p->stand_std[j];
+    k.walk[j] = p->walk_std[j];
+    k.soft[j][0] = p->soft_limits[j][0];
+    k.soft[j][1] = p->soft_limits[j][1];
+  }
+  return k;
+}
+
+template <class R> BamBuffers<R> bamBuffers(const duck_bam_buffers *x) {
+  require(x != nullptr, "Invalid arguments");
+  const void *need[] = {x->home, x->root_offset, x->zero_forces, x->action, x->old_action, x->previous_motor,
+                        x->previous_applied, x->observed_velocity, x->command, x->mean_velocity_world,
+                        x->target_yaw, x->self_contacts, x->self_penetration, x->air_time, x->contact_time,
+                        x->peak_height, x->contact_force, x->joints, x->head_ema, x->target_history, x->motor,
+                        x->features, x->terms, x->contact, x->history_initialized, x->done, x->timeout,
+                        x->failed, x->episode_length, x->counters, x->obs_actor, x->obs_critic, x->reward};
+  for (const void *ptr : need) require(ptr != nullptr, "Missing BAM buffer");
+  BamBuffers<R> B;
+  B.home = static_cast<const R *>(x->home);
+  B.rootOffset = static_cast<const R *>(x->root_offset);
+  B.action = static_cast<R *>(x->action);
+  B.oldAction = static_cast<R *>(x->old_action);
+  B.prevMotor = static_cast<R *>(x->previous_motor);
+  B.prevApplied = static_cast<R *>(x->previous_applied);
+  B.observedVelocity = static_cast<R *>(x->observed_velocity);
+  B.command = static_cast<R *>(x->command);
+  B.meanVelocity = static_cast<R *>(x->mean_velocity_world);
+  B.targetYaw = static_cast<R *>(x->target_yaw);
+  B.airTime = static_cast<R *>(x->air_time);
+  B.contactTime = static_cast<R *>(x->contact_time);
+  B.contactForce = static_cast<R *>(x->contact_force);
+  B.selfContacts = static_cast<R *>(x->self_contacts);
+  B.selfPenetration = static_cast<R *>(x->self_penetration);
+  B.joints = static_cast<R *>(x->joints);
+  B.headEma = static_cast<R *>(x->head_ema);
+  B.peakHeight = static_cast<R *>(x->peak_height);
+  B.history = static_cast<R *>(x->target_history);
+  B.motor = static_cast<R *>(x->motor);
+  B.features = static_cast<R *>(x->features);
+  B.terms = static_cast<R *>(x->terms);
+  B.contact = reinterpret_cast<bool *>(x->contact);
+  B.histInit = reinterpret_cast<bool *>(x->history_initialized);
+  B.done = reinterpret_cast<bool *>(x->done);
+  B.timeout = reinterpret_cast<bool *>(x->timeout);
+  B.failed = reinterpret_cast<bool *>(x->failed);
+  B.episodeLength = reinterpret_cast<long long *>(x->episode_length);
+  B.counters = x->counters;
+  B.obsActor = x->obs_actor;
+  B.obsCritic = x->obs_critic;
+  B.reward = x->reward;
+  return B;
+}
+
+enum BamPart { kBamBegin = 1, kBamSubstep = 2, kBamFinish = 4, kBamServoOnly = 8 };
+
+template <class R>
+void bamRun(duck_batch *b, const BamKernelParams &k, const duck_bam_buffers *x, const void *actions, int parts,
+            int substeps, cudaStream_t s) {
+  const BamBuffers<R> B = bamBuffers<R>(x);
+  const DevModel<R> *m = static_cast<const DevModel<R> *>(b->devModel);
+  const R *rec = static_cast<const R *>(b->records);
+  const int grid = blocksFor(b->n, 128);
+  if (parts & kBamBegin) {
+    bamBeginKernel<R><<<grid, 128, 0, s>>>(k, B, b->n, static_cast<const R *>(actions));
+    ++b->launches;
+  }
+  if (parts & kBamServoOnly) {
+    bamServoKernel<R><<<grid, 128, 0, s>>>(m, rec, b->recordStride, b->n, k, B);
+    ++b->launches;
+  }
+  if (parts & kBamSubstep) {
+    for (int i = 0; i < substeps; ++i) {
+      bamServoKernel<R><<<grid, 128, 0, s>>>(m, rec, b->recordStride, b->n, k, B);
+      StepArgs args{nullptr, x->zero_forces, x->motor, 1, 0.0, 0.0};
+      launchAdvance<R>(b, args, s);
+      bamAfterKernel<R><<<grid, 128, 0, s>>>(m, rec, b->recordStride, b->n, k, B);
+      b->launches += 2;
+    }
+  }
+  if (parts & kBamFinish) {
+    bamControlKernel<R><<<grid, 128, 0, s>>>(m, rec, b->recordStride, b->n, k, B, 0, nullptr);
+    ++b->launches;
+  }
+}
+
+int bamCall(duck_batch *b, const duck_bam_params *params, const duck_bam_buffers *x, const void *actions,
+            int parts, duck_stream stream) {
+  return guarded([&] {
+    require(b && x, "Invalid arguments");
+    require(!(parts & kBamBegin) || actions, "Missing actions");
+    const BamKernelParams k = bamParams(b, params);
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    begin(b, s);
+    if (b->fp64) bamRun<double>(b, k, x, actions, parts, params->decimation, s);
+    else bamRun<float>(b, k, x, actions, parts, params->decimation, s);
+    finish(b, s);
+  });
+}
+}  // namespace
+
+extern "C" {
+
+int duck_bam_critic_dim(const duck_batch *b, const duck_bam_params *p) {
+  if (!b || !p) return -1;
+  return 34 + 3 * b->nj + (p->mean_velocity ? 3 : 0) + (p->heading_reward ? 1 : 0);
+}
+
+int duck_bam_step(duck_batch *b, const duck_bam_params *p, const duck_bam_buffers *x, const void *actions,
+                  duck_stream stream) {
+  return bamCall(b, p, x, actions, kBamBegin | kBamSubstep | kBamFinish, stream);
+}
+
+int duck_bam_begin(duck_batch *b, const duck_bam_params *p, const duck_bam_buffers *x, const void *actions,
+                   duck_stream stream) {
+  return bamCall(b, p, x, actions, kBamBegin, stream);
+}
+
+int duck_bam_substep(duck_batch *b, const duck_bam_params *p, const duck_bam_buffers *x, duck_stream stream) {
+  if (!p) return bamCall(b, p, x, nullptr, 0, stream);
+  duck_bam_params one = *p;
+  one.decimation = 1;
+  return bamCall(b, &one, x, nullptr, kBamSubstep, stream);
+}
+
+int duck_bam_finish(duck_batch *b, const duck_bam_params *p, const duck_bam_buffers *x, duck_stream stream) {
+  return bamCall(b, p, x, nullptr, kBamFinish, stream);
+}
+
+int duck_bam_servo(duck_batch *b, const duck_bam_params *p, const duck_bam_buffers *x, duck_stream stream) {
+  return bamCall(b, p, x, nullptr, kBamServoOnly, stream);
+}
+
+int duck_bam_reset_buffers(duck_batch *b, const duck_bam_params *p, const duck_bam_buffers *x, const uint8_t *mask,
+                           duck_stream stream) {
+  return guarded([&] {
+    require(b && x && mask, "Invalid arguments");
+    const BamKernelParams k = bamParams(b, p);
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    auto run = [&](auto zero) {
+      using R = decltype(zero);
+      bamResetKernel<R><<<blocksFor(b->n, 128), 128, 0, s>>>(k, bamBuffers<R>(x), b->n,
+                                                              reinterpret_cast<const bool *>(mask));
+    };
+    if (b->fp64) run(0.0); else run(0.0f);
+    ++b->launches;
+    check(cudaGetLastError(), "bam reset buffers");
+  });
+}
+
+int duck_bam_observe(duck_batch *b, const duck_bam_params *p, const duck_bam_buffers *x, const uint8_t *mask,
+                     int update_heading, duck_stream stream) {
+  return guarded([&] {
+    require(b && x, "Invalid arguments");
+    const BamKernelParams k = bamParams(b, p);
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    begin(b, s);
+    auto run = [&](auto zero) {
+      using R = decltype(zero);
+      bamControlKernel<R><<<blocksFor(b->n, 128), 128, 0, s>>>(
+          static_cast<const DevModel<R> *>(b->devModel), static_cast<const R *>(b->records), b->recordStride, b->n,
+          k, bamBuffers<R>(x), update_heading ? 1 : 2, reinterpret_cast<const bool *>(mask));
+    };
+    if (b->fp64) run(0.0); else run(0.0f);
+    ++b->launches;
+    finish(b, s);
   });
 }
 

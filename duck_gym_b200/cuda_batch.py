@@ -74,12 +74,21 @@ def library():
         lib.duck_env_post_step.argtypes = [P] * 17
         lib.duck_env_observe.argtypes = [P] * 9
         lib.duck_env_reset_buffers.argtypes = [P] * 10
+        lib.duck_bam_critic_dim.argtypes = [P, P]
+        for name in ("duck_bam_step", "duck_bam_begin"):
+            getattr(lib, name).argtypes = [P, P, P, P, P]
+        for name in ("duck_bam_substep", "duck_bam_finish", "duck_bam_servo"):
+            getattr(lib, name).argtypes = [P, P, P, P]
+        lib.duck_bam_reset_buffers.argtypes = [P, P, P, P, P]
+        lib.duck_bam_observe.argtypes = [P, P, P, P, I, P]
         for name in ("duck_batch_create", "duck_batch_info", "duck_batch_reset", "duck_batch_step",
                      "duck_batch_step_motor", "duck_batch_state", "duck_batch_contact_forces",
                      "duck_batch_self_contact_stats", "duck_batch_contact_counts",
                      "duck_batch_generalized_loads", "duck_batch_reference", "duck_batch_export",
                      "duck_batch_import", "duck_batch_contact_keys", "duck_fp32_peak", "duck_env_obs_dim",
-                     "duck_env_targets", "duck_env_post_step", "duck_env_observe", "duck_env_reset_buffers"):
+                     "duck_env_targets", "duck_env_post_step", "duck_env_observe", "duck_env_reset_buffers",
+                     "duck_bam_critic_dim", "duck_bam_step", "duck_bam_begin", "duck_bam_substep", "duck_bam_finish",
+                     "duck_bam_servo", "duck_bam_reset_buffers", "duck_bam_observe"):
             getattr(lib, name).restype = I
         _lib = lib
     return _lib

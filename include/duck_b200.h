@@ -186,6 +186,90 @@ int duck_env_reset_buffers(duck_batch *batch, const uint8_t *mask, void *prev_ac
                            int64_t *episode_length, float *returns, void *filtered, void *commands,
                            const void *new_commands, duck_stream stream);
 
+/* BAM environment (the reference's python/duck_gym/bam_env.py with the
+ * XL330/m6 servo of actuator.py:16-77 and the walking reward of
+ * walking_reward.py) fused into kernels that read the batch's physics state
+ * directly.  Settings come from the env's config.json and training dictionary
+ * (bam_env.py:33-133).  J <= 32, two feet. */
+typedef struct duck_bam_params {
+  int lag, decimation, max_episode_length, source_iteration;
+  int neutral_head, heading_hold, reward_enabled;
+  int head_stability, mean_velocity, heading_reward; /* optional terms (bam_env.py:358-381) */
+  int foot_body[2];
+  uint32_t head_mask;     /* bit j: joint j is a head or neck joint */
+  uint32_t override_mask; /* bit t: walking weight t replaced by overrides[t] */
+  double dt, step_dt;     /* physics and control step */
+  double kp_fw, vin, vin_drop_gain, vin_min, force_limit;
+  double kt, R, friction_base, friction_stribeck, load_friction_external, load_friction_motor,
+      load_friction_external_stribeck, load_friction_motor_stribeck, load_friction_external_quad,
+      load_friction_motor_quad, dtheta_stribeck, alpha, friction_viscous;
+  double root_iquat[4];   /* conjugated root principal-frame quaternion */
+  double foot_site[2][3]; /* sole sites in foot-body coordinates */
+  double linear_variance, vertical_variance, mean_velocity_alpha, mean_velocity_variance,
+      mean_velocity_weight, heading_reward_weight, heading_reward_variance, head_position_weight,
+      head_velocity_weight;
+  double tilt_limit;      /* -cos(70 deg) */
+  double overrides[15];   /* walking weights in walking_reward.py:108-122 order */
+  double stand_std[32], walk_std[32], soft_limits[32][2];
+} duck_bam_params;
+
+/* Device buffers of one BAM environment batch ([E,...], Real unless noted).
+ * Names follow the reference BamEnv attributes. */
+typedef struct duck_bam_buffers {
+  const void *home, *root_offset, *zero_forces;     /* [E,J], [E,3], [E,3] zeros */
+  void *action, *old_action, *previous_motor, *previous_applied, *observed_velocity; /* [E,J] */
+  void *command, *mean_velocity_world;             /* [E,3] */
+  void *target_yaw, *self_contacts, *self_penetration; /* [E] */
+  void *air_time, *contact_time, *peak_height;     /* [E,2] */
+  void *contact_force;                             /* [E,2,3] */
+  void *joints;                                    /* [E,J,2] */
+  void *head_ema;                                  /* [E,4] */
+  void *target_history;                            /* [lag+1,E,J] */
+  void *motor;                                     /* [E,J,3] scratch: motor channels */
+  void *features;                                  /* [E,29]: root quat, gravity, ang_vel, lin_vel,
+                                                      root-origin world velocity, site pos [2,3],
+                                                      site vel [2,3], numeric-failure flag */
+  void *terms;                                     /* [E,19] reward terms */
+  uint8_t *contact, *history_initialized;          /* bool [E,2], [E] */
+  uint8_t *done, *timeout, *failed;                /* bool [E] */
+  int64_t *episode_length;                         /* [E] */
+  int32_t *counters;                               /* [2]: delay-ring cursor, common step counter */
+  float *obs_actor, *obs_critic, *reward;          /* [E,19+3J], [E,duck_bam_critic_dim], [E] */
+} duck_bam_buffers;
+
+/* Critic observation width (76 for 14 joints, +3 with the mean-velocity
+ * filter, +1 with the heading reward). */
+int duck_bam_critic_dim(const duck_batch *batch, const duck_bam_params *params);
+/* bam_env.py:292-389: one control step -- prologue, decimation x (servo,
+ * one physics substep, bookkeeping), reward, masks and observations.
+ * actions [E,J] Real.  Launches only kernels (no host synchronisation), so
+ * the sequence can be captured into a CUDA graph. */
+int duck_bam_step(duck_batch *batch, const duck_bam_params *params, const duck_bam_buffers *buffers,
+                  const void *actions, duck_stream stream);
+/* The parts of duck_bam_step, for per-substep callbacks:
+ * begin (:292-303), one substep (:305-344), finish (:345-389). */
+int duck_bam_begin(duck_batch *batch, const duck_bam_params *params, const duck_bam_buffers *buffers,
+                   const void *actions, duck_stream stream);
+int duck_bam_substep(duck_batch *batch, const duck_bam_params *params, const duck_bam_buffers *buffers,
+                     duck_stream stream);
+int duck_bam_finish(duck_batch *batch, const duck_bam_params *params, const duck_bam_buffers *buffers,
+                    duck_stream stream);
+/* The servo alone (delay ring, generalized loads, XL330/m6) writing the motor
+ * channels of one substep without stepping the physics. */
+int duck_bam_servo(duck_batch *batch, const duck_bam_params *params, const duck_bam_buffers *buffers,
+                   duck_stream stream);
+/* bam_env.py:245-275: zero the buffers of the masked environments and refill
+ * their delay ring with HOME (the physics reset is duck_batch_reset). */
+int duck_bam_reset_buffers(duck_batch *batch, const duck_bam_params *params,
+                           const duck_bam_buffers *buffers, const uint8_t *mask, duck_stream stream);
+/* bam_env.py:136-211: refresh frames (features, joints, foot contacts) and
+ * observations from the current physics state.  With update_heading set (the
+ * end of reset, :270-275) the masked environments (mask may be NULL) first
+ * take their current heading as target and the heading command is updated
+ * when heading hold is on. */
+int duck_bam_observe(duck_batch *batch, const duck_bam_params *params, const duck_bam_buffers *buffers,
+                     const uint8_t *mask, int update_heading, duck_stream stream);
+
 /* No reference counterpart.  Number of kernel launches issued by this batch
  * since creation (for launch accounting in benchmarks). */
 int64_t duck_batch_launches(const duck_batch *batch);

@@ -11,7 +11,7 @@ import helpers
 from oracle.oracle import OracleBatch, count_ops, reference_module
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("env_"))   # env_*: tensor-env fixtures
+CASES = sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("env_", "bam_")))   # env fixtures
 
 
 @pytest.mark.parametrize("case", CASES)

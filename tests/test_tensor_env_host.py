@@ -33,3 +33,40 @@ def test_params_layout_matches_header():
     names = re.findall(r"\b([a-z_]+)(?:\[4\])?\s*[,;]", re.sub(r"/\*.*?\*/", "", body, flags=re.S))
     assert [n for n, _ in EnvParams._fields_] == names
     assert ctypes.sizeof(EnvParams) == 4 * 3 + 4 + 8 * 8 + 8 * 4
+
+
+def _struct_fields(name):
+    import re
+    from pathlib import Path
+
+    header = (Path(__file__).resolve().parents[1] / "include" / "duck_b200.h").read_text()
+    body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (name, name), header, re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    fields = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if not decl:
+            continue
+        names = decl.split(None, 1)[1] if not decl.startswith("const ") else decl.split(None, 2)[2]
+        for item in names.split(","):
+            fields.append(re.sub(r"[\s*]|\[.*", "", item))
+    return fields
+
+
+def test_bam_structs_match_header():
+    import ctypes
+
+    from duck_gym_b200.bam_env import BamBufferTable, BamParams
+
+    assert [n for n, _ in BamParams._fields_] == _struct_fields("duck_bam_params")
+    assert [n for n, _ in BamBufferTable._fields_] == _struct_fields("duck_bam_buffers")
+    assert ctypes.sizeof(BamBufferTable) == 8 * len(BamBufferTable._fields_)
+
+
+def test_bam_env_rejects_cpu_backend(tmp_path):
+    from duck_gym_b200 import biped
+    from duck_gym_b200.bam_env import BamEnv
+
+    biped.write_bam(tmp_path, seed=0)
+    with pytest.raises(ValueError):
+        BamEnv(tmp_path, backend="cpu")
