@@ -300,6 +300,8 @@ HostModel<R> convertModel(const ParsedModel &o, double dt, int iterations, bool 
     d.sFriction[i] = R(s.friction); d.sRadius[i] = R(s.boundingRadius);
     d.sOffset[i] = int(h.points.size() / 3);
     d.sCount[i] = s.type == 0 ? 1 : (s.type == 2 ? 2 : int(s.localPoints.size()));
+    // Warm-start keys pack (shape, point) into 10 + 20 bits.
+    if (d.sCount[i] >= (1 << 20)) throw std::invalid_argument("Collision shape has too many points");
     DVec interior = s.center;
     if (!s.localPoints.empty()) {
       interior = {};

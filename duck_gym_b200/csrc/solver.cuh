@@ -50,7 +50,7 @@ struct Layout {
   int JL, JP, JC0, JA0, JV0, JLF, JPF, JT, JTQ, JFL, JD;  // joints
   int C, CB;                                           // contacts, self-contact basis
   int I;                                               // ints (Real slot offset)
-  int colors, colorList, colorStart, masks;            // offsets inside the int region
+  int colors, colorList, colorStart, masks, prevKeys;  // offsets inside the int region
   int cap, pairCap, maxColors;
   int size;                                            // Reals per environment
 };
@@ -74,8 +74,10 @@ template <class R> __host__ inline Layout makeLayout(const DevModel<R> &m) {
   L.colorList = iMisc + nb;
   L.colorStart = iMisc + 2 * nb;
   L.masks = L.colorStart + L.maxColors + 1;
+  // Ground keys of the previous substep's contacts (warm-start lookup).
+  L.prevKeys = L.masks + 2 * nb;
   // One Real slot per integer keeps the interleaved addressing uniform.
-  L.I = take(L.masks + 2 * nb);
+  L.I = take(L.prevKeys + std::max(L.cap, 1));
   L.size = o;
   return L;
 }
@@ -135,6 +137,10 @@ struct StepArgs {
 template <class R, int T> struct Solver {
   static constexpr int kTeams = 32 / T;
   static constexpr int kPerLane = (kMaxBodies + T - 1) / T;   // bodies per lane in lane-per-body loops
+  // Lanes that share one body's block update in the Gauss-Seidel sweep: with
+  // 16 or more lanes per environment a colour's bodies outnumber half the
+  // team at most, so each body gets two lanes that split its rows.
+  static constexpr int kSplit = T >= 16 ? 2 : 1;
   using SV = View<R, kTeams>;
   const DevModel<R> *__restrict__ m;
   const R *__restrict__ pts;
@@ -310,26 +316,67 @@ template <class R, int T> struct Solver {
     if (double(xsub(low, xmul(ldg(m->sRadius[s]), xadd(R(1), xmul(dt, xnorm(w)))))) >= .003) return 0;
     const int count = ldg(m->sCount[s]);
     int n = 0;
+    // Up to 4 picks of the lowest predicted points below 3 mm, 5 mm apart
+    // laterally.  Shapes of at most 8 points (spheres, capsules, boxes) keep
+    // their world points and predicted heights in registers across the picks;
+    // larger point sets recompute them per pick.  Either way every point is
+    // evaluated with the same arithmetic, so the picks are identical.
+    auto point = [&](int k, V3<R> &wp) {
+      V3<R> local = xpoint(s, q, k);
+      wp = xadd(x, xrotate(q, local));
+      V3<R> vv = xadd(v, xcross(w, xsub(wp, x)));
+      return rmin(wp.z, xadd(xadd(wp.z, xmul(dt, vv.z)), xmul(dt2, accel)));
+    };
+    auto accept = [&](V3<R> wp) {
+      bool ok = true;
+#pragma unroll
+      for (int c = 0; c < 3; ++c)
+        if (c < n && double(xhypot(xsub(world[c].x, wp.x), xsub(world[c].y, wp.y))) < .005) ok = false;
+      return ok;
+    };
+    if (count <= 8) {
+      V3<R> wps[8];
+      R zs[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < count) zs[k] = point(k, wps[k]);
+      for (int pick = 0; pick < 4; ++pick) {
+        int best = -1;
+        R lowest = R(INFINITY);
+        V3<R> bestWorld{};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (k >= count) continue;
+          const R z = zs[k];
+          if (double(z) >= .003 || z >= lowest || !accept(wps[k])) continue;
+          best = k;
+          lowest = z;
+          bestWorld = wps[k];
+        }
+        if (best < 0) break;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (c == n) { feature[c] = best; world[c] = bestWorld; }
+        ++n;
+      }
+      return n;
+    }
     for (int pick = 0; pick < 4; ++pick) {
       int best = -1;
       R lowest = R(INFINITY);
       V3<R> bestWorld{};
       for (int k = 0; k < count; ++k) {
-        V3<R> local = xpoint(s, q, k), wp = xadd(x, xrotate(q, local));
-        V3<R> vv = xadd(v, xcross(w, xsub(wp, x)));
-        R z = rmin(wp.z, xadd(xadd(wp.z, xmul(dt, vv.z)), xmul(dt2, accel)));
-        if (double(z) >= .003 || z >= lowest) continue;
-        bool duplicate = false;
-        for (int c = 0; c < n; ++c)
-          if (double(xhypot(xsub(world[c].x, wp.x), xsub(world[c].y, wp.y))) < .005) duplicate = true;
-        if (duplicate) continue;
+        V3<R> wp;
+        const R z = point(k, wp);
+        if (double(z) >= .003 || z >= lowest || !accept(wp)) continue;
         best = k;
         lowest = z;
         bestWorld = wp;
       }
       if (best < 0) break;
-      feature[n] = best;
-      world[n] = bestWorld;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c == n) { feature[c] = best; world[c] = bestWorld; }
       ++n;
     }
     return n;
@@ -343,9 +390,10 @@ template <class R, int T> struct Solver {
     V3<R> anchor{bestWorld.x, bestWorld.y, R(0)};
     R lambda[3] = {R(0), R(0), R(0)}, penalty[3] = {R(1000), R(1000), R(1000)};
     const R *prev = rec + kRecHeader + kRecBody * m->nb + kRecJoint * m->nj;
+    const int key = groundKey(s, best);
     for (int i = 0; i < prevCount; ++i) {
-      const R *p = prev + kRecContact * i;
-      if (p[3] < R(0) && int(p[1]) == s && int(p[2]) == best) {
+      if (I[L.prevKeys + i] == key) {
+        const R *p = prev + kRecContact * i;
 #pragma unroll
         for (int d = 0; d < 3; ++d) { lambda[d] = p[26 + d]; penalty[d] = p[29 + d]; }
         if (p[5] != R(0)) {
@@ -373,11 +421,24 @@ template <class R, int T> struct Solver {
 
 #include "mpr.cuh"
 
+  // Warm-start key of a ground contact: shape and feature (point index).
+  static __device__ __forceinline__ int groundKey(int shape, int feature) { return shape << 20 | feature; }
+
   __device__ void detectContacts() {
     const int nb = m->nb;
     for (int b = team.lane; b < nb; b += T) I[L.colors + b] = ldg(m->color[b]);
     if (team.lane == 0) I[iColors] = 2;
     const int prevCount = I[iPrevCount];
+    // Stage the keys of the previous substep's contacts from the record, one
+    // lane per contact, so the lookups below search shared memory.
+    {
+      const R *prev = rec + kRecHeader + kRecBody * m->nb + kRecJoint * m->nj;
+      for (int i = team.lane; i < prevCount; i += T) {
+        const R *p = prev + kRecContact * i;
+        I[L.prevKeys + i] = p[3] < R(0) ? groundKey(int(p[1]), int(p[2])) : -1;
+      }
+      team.sync();
+    }
     int base = 0;
     for (int first = 0; first < m->ns; first += T) {
       const int s = first + team.lane;
@@ -386,7 +447,9 @@ template <class R, int T> struct Solver {
       int n = s < m->ns ? groundPicks(s, feature, world) : 0;
       int total;
       int offset = team.scan(n, &total);
-      for (int k = 0; k < n; ++k) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (k >= n) break;
         int slot = base + offset + k;
         if (slot < L.cap) buildGround(slot, s, feature[k], world[k], prevCount);
         else I[iFailed] = 1;
@@ -604,9 +667,78 @@ template <class R, int T> struct Solver {
   }
 
   // ------------------------------------------------------------ primal
-  // Block update of body bi (kernel.cuh:828-936).
-  __device__ R updateBody(int bi, R kp, R limit) {
+  // Rows of hinge j acting on body bi (kernel.cuh:863-913): anchor rows with
+  // their geometric stiffness, axis-orthogonality rows, then limits, PD drive,
+  // damping/armature and dry friction summed along the hinge axis.
+  __device__ __forceinline__ void stampHinge(int bi, int j, const JointGeo &e, R *H, R *g, R kp, R limit) const {
     const R h = m->dt, alpha = m->alpha;
+    const R ih = R(1) / h, ih2 = ih * ih;
+    const bool parent = e.a == bi;
+    const R s = parent ? R(1) : R(-1);
+    const SV lam = S + (L.JL + 7 * j), pen = S + (L.JP + 7 * j), c0 = S + (L.JC0 + 7 * j);
+    const V3<R> r = parent ? e.ra : e.rb;
+    R f3[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      R c = e.C[k] - alpha * c0[k];
+      R f = lam[k] + pen[k] * c;
+      f3[k] = f;
+      stampLinear(H, g, k, r, s * f, pen[k]);
+    }
+    // Anchor rows: lever (parent ? ra : -rb) under unit-axis forces f_k e_k;
+    // the majorizer depends on the lever only through its squares.
+    geometricAxes(H, r, f3[0], f3[1], f3[2]);
+#pragma unroll
+    for (int k = 3; k < 5; ++k) {
+      R c = e.C[k] - alpha * c0[k];
+      R f = lam[k] + pen[k] * c;
+      V3<R> t = k == 3 ? e.t1 : e.t2;
+      stampAngular(H, g, cross(t, e.axisB) * s, f, pen[k]);
+      geometric(H, parent ? t : e.axisB, (parent ? e.axisB : t) * f);
+    }
+    // Every remaining row acts along the hinge axis: J = (0, -s axis).
+    R stiff = R(0), force = R(0);
+    if (e.limited) {
+      R c5 = e.C[5] - alpha * rmin(c0[5], R(0));
+      R f5 = rmin(lam[5] + pen[5] * c5, R(0));
+      if (f5 < R(0)) { stiff += pen[5]; force += f5; }
+      R c6 = e.C[6] - alpha * rmin(c0[6], R(0));
+      R f6 = rmin(lam[6] + pen[6] * c6, R(0));
+      if (f6 < R(0)) { stiff += pen[6]; force -= f6; }
+    }
+    R drive = kp * wrapAngle(e.angle - S[L.JT + j]) - S[L.JTQ + j];
+    R driveStiffness = kp;
+    if (limit > R(0)) {
+      if (fabs(drive) >= limit) driveStiffness = R(0);
+      drive = rclamp(drive, -limit, limit);
+    }
+    stiff += driveStiffness;
+    force += drive;
+    const R damping = S[L.JD + j], armature = ldg(m->armature[j]);
+    const R delta = wrapAngle(e.angle - S[L.JA0 + j]);
+    const R dstiff = damping * ih + armature * ih2;
+    if (dstiff > R(0)) {
+      stiff += dstiff;
+      force += damping * ih * delta + armature * ih2 * (delta - h * S[L.JV0 + j]);
+    }
+    const R fl = S[L.JFL + j];
+    if (fl > R(0)) {
+      R trial = S[L.JLF + j] + S[L.JPF + j] * delta;
+      force += rclamp(trial, -fl, fl);
+      if (fabs(trial) < fl) stiff += S[L.JPF + j];
+    }
+    stampAngular(H, g, e.axis * (-s), force, stiff);
+  }
+
+  // Block update of body bi (kernel.cuh:828-936).
+  // With kSplit = 2 the two lanes of a pair (part 0 and 1) take alternate
+  // items -- the inertia block, then each hinge, then each contact -- and
+  // add their partial H and g with one shuffle per entry; both then solve
+  // the same system and part 0 writes the pose.
+  __device__ R updateBody(int bi, R kp, R limit, int part = 0) {
+    const R h = m->dt, alpha = m->alpha;
+    int item = 0;
+    auto mine = [&]() { return kSplit == 1 || (item++ & 1) == part; };
     const R ih = R(1) / h, ih2 = ih * ih;
     const R mass = ldg(m->mass[bi]);
     R H[21], g[6];
@@ -617,7 +749,7 @@ template <class R, int T> struct Solver {
     const V3<R> x = ld3(L.X + 3 * bi), xp = ld3(L.XQP + 7 * bi);
     const Q4<R> q = quat(bi), qp = ld4(L.XQP + 7 * bi + 3);
     // Inertia block with the SO(3) log Jacobian and frozen world inertia.
-    {
+    if (mine()) {
       V3<R> dx = x - xp, th = fqlog(qmul(q, conj(qp)));
       R ml = mass * ih2;
       H[tri(0, 0)] = ml; H[tri(1, 1)] = ml; H[tri(2, 2)] = ml;
@@ -654,72 +786,34 @@ template <class R, int T> struct Solver {
           H[tri(3 + k, 3 + l)] = (J[0][k] * N[0][l] + J[1][k] * N[1][l] + J[2][k] * N[2][l]) * ih2;
       }
     }
-    // Hinges touching bi, in CSR order.
-    const int adjEnd = ldg(m->csrOffset[bi + 1]);
-    for (int adj = ldg(m->csrOffset[bi]); adj < adjEnd; ++adj) {
-      const int j = ldg(m->csrJoint[adj]);
-      JointGeo e;
-      evalJoint(j, e);
-      const bool parent = e.a == bi;
-      const R s = parent ? R(1) : R(-1);
-      const SV lam = S + (L.JL + 7 * j), pen = S + (L.JP + 7 * j), c0 = S + (L.JC0 + 7 * j);
-      const V3<R> r = parent ? e.ra : e.rb;
-      R f3[3];
-#pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        R c = e.C[k] - alpha * c0[k];
-        R f = lam[k] + pen[k] * c;
-        f3[k] = f;
-        stampLinear(H, g, k, r, s * f, pen[k]);
+    // Hinges touching bi, in CSR order.  Without a split, two hinges are
+    // evaluated side by side: their geometry chains (rotations, atan2) are
+    // independent, which gives the scheduler two streams to interleave.
+    const int adjBegin = ldg(m->csrOffset[bi]), adjEnd = ldg(m->csrOffset[bi + 1]);
+    if constexpr (kSplit == 1) {
+      for (int adj = adjBegin; adj < adjEnd; adj += 2) {
+        const bool two = adj + 1 < adjEnd;
+        const int j0 = ldg(m->csrJoint[adj]), j1 = ldg(m->csrJoint[two ? adj + 1 : adj]);
+        JointGeo e0, e1;
+        evalJoint(j0, e0);
+        evalJoint(j1, e1);
+        stampHinge(bi, j0, e0, H, g, kp, limit);
+        if (two) stampHinge(bi, j1, e1, H, g, kp, limit);
       }
-      // Anchor rows: lever (parent ? ra : -rb) under unit-axis forces f_k e_k;
-      // the majorizer depends on the lever only through its squares.
-      geometricAxes(H, r, f3[0], f3[1], f3[2]);
-#pragma unroll
-      for (int k = 3; k < 5; ++k) {
-        R c = e.C[k] - alpha * c0[k];
-        R f = lam[k] + pen[k] * c;
-        V3<R> t = k == 3 ? e.t1 : e.t2;
-        stampAngular(H, g, cross(t, e.axisB) * s, f, pen[k]);
-        geometric(H, parent ? t : e.axisB, (parent ? e.axisB : t) * f);
+    } else {
+      for (int adj = adjBegin; adj < adjEnd; ++adj) {
+        if (!mine()) continue;
+        const int j = ldg(m->csrJoint[adj]);
+        JointGeo e;
+        evalJoint(j, e);
+        stampHinge(bi, j, e, H, g, kp, limit);
       }
-      // Every remaining row acts along the hinge axis: J = (0, -s axis).
-      R stiff = R(0), force = R(0);
-      if (e.limited) {
-        R c5 = e.C[5] - alpha * rmin(c0[5], R(0));
-        R f5 = rmin(lam[5] + pen[5] * c5, R(0));
-        if (f5 < R(0)) { stiff += pen[5]; force += f5; }
-        R c6 = e.C[6] - alpha * rmin(c0[6], R(0));
-        R f6 = rmin(lam[6] + pen[6] * c6, R(0));
-        if (f6 < R(0)) { stiff += pen[6]; force -= f6; }
-      }
-      R drive = kp * wrapAngle(e.angle - S[L.JT + j]) - S[L.JTQ + j];
-      R driveStiffness = kp;
-      if (limit > R(0)) {
-        if (fabs(drive) >= limit) driveStiffness = R(0);
-        drive = rclamp(drive, -limit, limit);
-      }
-      stiff += driveStiffness;
-      force += drive;
-      const R damping = S[L.JD + j], armature = ldg(m->armature[j]);
-      const R delta = wrapAngle(e.angle - S[L.JA0 + j]);
-      const R dstiff = damping * ih + armature * ih2;
-      if (dstiff > R(0)) {
-        stiff += dstiff;
-        force += damping * ih * delta + armature * ih2 * (delta - h * S[L.JV0 + j]);
-      }
-      const R fl = S[L.JFL + j];
-      if (fl > R(0)) {
-        R trial = S[L.JLF + j] + S[L.JPF + j] * delta;
-        force += rclamp(trial, -fl, fl);
-        if (fabs(trial) < fl) stiff += S[L.JPF + j];
-      }
-      stampAngular(H, g, e.axis * (-s), force, stiff);
     }
     // Contacts touching bi, in list order.
     const int nGround = I[iGround];
     const SV Rb = rot(bi);
     auto touch = [&](int ci) {
+      if (!mine()) return;
       const int meta = cmeta(ci);
       const int body = metaBody(meta), other = metaOther(meta);
       const SV c = contact(ci);
@@ -769,6 +863,13 @@ template <class R, int T> struct Solver {
         if (metaBody(meta) == bi || metaOther(meta) == bi) touch(ci);
       }
     }
+    if constexpr (kSplit == 2) {
+      const unsigned pair = 3u << ((threadIdx.x & 31) & ~1);
+#pragma unroll
+      for (int i = 0; i < 21; ++i) H[i] += __shfl_xor_sync(pair, H[i], 1);
+#pragma unroll
+      for (int i = 0; i < 6; ++i) g[i] += __shfl_xor_sync(pair, g[i], 1);
+    }
     R st[6];
     if (!solve(H, g, st)) {
 #pragma unroll
@@ -777,8 +878,38 @@ template <class R, int T> struct Solver {
     V3<R> tx{st[0], st[1], st[2]}, rx{st[3], st[4], st[5]};
     R nt = fnorm(tx), nr = fnorm(rx);
     R scale = rmin(R(1), rmin(R(.1) * frcp(rmax(nt, R(1e-30))), R(.25) * frcp(rmax(nr, R(1e-30)))));
-    setPose(bi, x + tx * scale, fnormalized(qmul(fqexp(rx * scale), q)));
+    if (part == 0) setPose(bi, x + tx * scale, fnormalized(qmul(fqexp(rx * scale), q)));
     return rmax(nt, nr) * scale;
+  }
+
+  // Dual update of hinge j (kernel.cuh:991-1028): multipliers, penalty ramps,
+  // dry friction; folds the constraint error into *error.
+  __device__ __forceinline__ void dualHinge(int j, const JointGeo &e, R &error) const {
+    const R alpha = m->alpha;
+    const SV lam = S + (L.JL + 7 * j), pen = S + (L.JP + 7 * j), c0 = S + (L.JC0 + 7 * j);
+    const int rows = e.limited ? 7 : 5;
+#pragma unroll
+    for (int k = 0; k < 7; ++k) {
+      if (k >= rows) break;
+      R c = e.C[k] - alpha * (k < 5 ? c0[k] : rmin(c0[k], R(0)));
+      R f = lam[k] + pen[k] * c;
+      lam[k] = k >= 5 ? rmin(f, R(0)) : f;
+      if (k < 5 || f < R(0))
+        pen[k] = rmin(pen[k] + (k < 3 ? m->betaLinear : m->betaAngular) * fabs(c), k < 3 ? R(1e9) : R(1e7));
+      error = rmax(error, k < 5 ? R(fabs(c)) : rmax(R(0), -c));
+    }
+    const R fl = S[L.JFL + j];
+    if (fl > R(0)) {
+      R delta = wrapAngle(e.angle - S[L.JA0 + j]);
+      R trial = S[L.JLF + j] + S[L.JPF + j] * delta;
+      R lf = rclamp(trial, -fl, fl);
+      R pf = S[L.JPF + j];
+      if (fabs(trial) < fl) pf = rmin(pf + m->betaAngular * R(fabs(delta)), R(1e7));
+      S[L.JLF + j] = lf;
+      S[L.JPF + j] = pf;
+      R residual = lf + pf * delta;
+      error = rmax(error, R(fabs(lf - rclamp(residual, -fl, fl))) * frcp(pf));
+    }
   }
 
   // Contact gap C in the contact basis, C.z shifted by -alpha c0 (kernel.cuh:805-827).
@@ -893,40 +1024,23 @@ template <class R, int T> struct Solver {
           begin = ldg(m->colorStart[color]);
           end = ldg(m->colorStart[color + 1]);
         }
-        for (int slot = begin + team.lane; slot < end; slot += T) {
+        for (int slot = begin + team.lane / kSplit; slot < end; slot += T / kSplit) {
           const int bi = m->np > 0 ? I[L.colorList + slot] : ldg(m->colorBody[slot]);
-          maxUpdate = rmax(maxUpdate, updateBody(bi, kp, limit));
+          maxUpdate = rmax(maxUpdate, updateBody(bi, kp, limit, team.lane % kSplit));
         }
         team.sync();
       }
       maxUpdate = team.max(maxUpdate);
       R error = R(0);
-      // Joint multipliers, penalties and dry friction (kernel.cuh:991-1028).
-      for (int j = team.lane; j < nj; j += T) {
-        JointGeo e;
-        evalJoint(j, e);
-        const SV lam = S + (L.JL + 7 * j), pen = S + (L.JP + 7 * j), c0 = S + (L.JC0 + 7 * j);
-        const int rows = e.limited ? 7 : 5;
-        for (int k = 0; k < rows; ++k) {
-          R c = e.C[k] - alpha * (k < 5 ? c0[k] : rmin(c0[k], R(0)));
-          R f = lam[k] + pen[k] * c;
-          lam[k] = k >= 5 ? rmin(f, R(0)) : f;
-          if (k < 5 || f < R(0))
-            pen[k] = rmin(pen[k] + (k < 3 ? m->betaLinear : m->betaAngular) * fabs(c), k < 3 ? R(1e9) : R(1e7));
-          error = rmax(error, k < 5 ? R(fabs(c)) : rmax(R(0), -c));
-        }
-        const R fl = S[L.JFL + j];
-        if (fl > R(0)) {
-          R delta = wrapAngle(e.angle - S[L.JA0 + j]);
-          R trial = S[L.JLF + j] + S[L.JPF + j] * delta;
-          R lf = rclamp(trial, -fl, fl);
-          R pf = S[L.JPF + j];
-          if (fabs(trial) < fl) pf = rmin(pf + m->betaAngular * R(fabs(delta)), R(1e7));
-          S[L.JLF + j] = lf;
-          S[L.JPF + j] = pf;
-          R residual = lf + pf * delta;
-          error = rmax(error, R(fabs(lf - rclamp(residual, -fl, fl))) * frcp(pf));
-        }
+      // Joint multipliers, penalties and dry friction (kernel.cuh:991-1028),
+      // two hinges per lane evaluated side by side.
+      for (int j = team.lane; j < nj; j += 2 * T) {
+        const bool two = j + T < nj;
+        JointGeo e0, e1;
+        evalJoint(j, e0);
+        evalJoint(two ? j + T : j, e1);
+        dualHinge(j, e0, error);
+        if (two) dualHinge(j + T, e1, error);
       }
       // Contact multipliers, stick flags and penalties (kernel.cuh:1029-1052).
       const int n = I[iCount], nGround = I[iGround];
@@ -1028,9 +1142,9 @@ template <class R, int T> struct Solver {
 // One launch advances every environment: target/forces (step) or motor/forces
 // (step_motor), then `substeps` physics steps with all state on chip.
 template <class R, int T>
-__global__ void __launch_bounds__(32) advanceKernel(const DevModel<R> *__restrict__ model,
+__global__ void __launch_bounds__(32, T >= 16 ? 14 : 1) advanceKernel(const DevModel<R> *__restrict__ model,
                                                     const R *__restrict__ points, R *records,
-                                                    int recordStride, int count, Layout L,
+                                                    int recordStride, int count, const __grid_constant__ Layout L,
                                                     StepArgs args) {
   extern __shared__ __align__(16) unsigned char smemRaw[];
   constexpr int teams = 32 / T;
