@@ -99,7 +99,7 @@ static __device__ V3<R> xportalPosition(const Sup *p, V3<R> d) {
 }
 // convexContact (convex.cuh:124-217) with bounded iterations: status 0
 // separated, 1 intersecting, -1 indeterminate.
-__device__ __noinline__ Hit xconvexContact(int sa, int sb, R inflation, R tolerance) const {
+__device__ __forceinline__ Hit xconvexContact(int sa, int sb, R inflation, R tolerance) const {
   Hit result{0, {R(0), R(0), R(0)}, {R(0), R(0), R(0)}, R(0)};
   const int ba = ldg(m->sBody[sa]), bb = ldg(m->sBody[sb]);
   Sup p[4];
@@ -172,7 +172,7 @@ __device__ __noinline__ Hit xconvexContact(int sa, int sb, R inflation, R tolera
 
 // Self-contact generation and warm start (kernel.cuh:654-722); returns the
 // new contact count.  Contacts follow the ground contacts in pair order.
-__device__ __noinline__ int detectPairs(int base, int prevCount) {
+__device__ __forceinline__ int detectPairs(int base, int prevCount) {
   const R dt = m->dt;
   const R tolerance = rmax(R(1e-8), xmul(m->tolerance, R(.1)));
   const R ag = xmul(m->alpha, m->gamma);

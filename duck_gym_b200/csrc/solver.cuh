@@ -301,9 +301,25 @@ template <class R, int T> struct Solver {
     V3<R> off = xrotate(mq4(m->sQ[s]), V3<R>{R(0), R(0), xmul(R(k ? 1 : -1), size.y)});
     return xadd(xadd(center, off), down);
   }
+  // World point k of shape s and its predicted height (kernel.cuh:614-630).
+  __device__ __forceinline__ R pickPoint(int s, int k, V3<R> x, V3<R> v, V3<R> w, Q4<R> q, R dt, R dt2, R accel,
+                                         V3<R> &wp) const {
+    V3<R> local = xpoint(s, q, k);
+    wp = xadd(x, xrotate(q, local));
+    V3<R> vv = xadd(v, xcross(w, xsub(wp, x)));
+    return rmin(wp.z, xadd(xadd(wp.z, xmul(dt, vv.z)), xmul(dt2, accel)));
+  }
+  // A candidate pick must lie 5 mm or more (laterally) from the earlier ones.
+  static __device__ __forceinline__ bool pickApart(V3<R> wp, const V3<R> *world, int n) {
+    bool ok = true;
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+      if (c < n && double(xhypot(xsub(world[c].x, wp.x), xsub(world[c].y, wp.y))) < .005) ok = false;
+    return ok;
+  }
   // Up to four lowest, laterally separated support points of shape s that are
   // predicted below 3 mm (kernel.cuh:338-364, 601-653), on one lane.
-  __device__ int groundPicks(int s, int *feature, V3<R> *world) const {
+  __device__ __forceinline__ int groundPicks(int s, int *feature, V3<R> *world) const {
     const int b = ldg(m->sBody[s]);
     const R mass = ldg(m->mass[b]);
     if (!m->ground || !ldg(m->sGround[s]) || mass == R(0)) return 0;
@@ -321,25 +337,12 @@ template <class R, int T> struct Solver {
     // their world points and predicted heights in registers across the picks;
     // larger point sets recompute them per pick.  Either way every point is
     // evaluated with the same arithmetic, so the picks are identical.
-    auto point = [&](int k, V3<R> &wp) {
-      V3<R> local = xpoint(s, q, k);
-      wp = xadd(x, xrotate(q, local));
-      V3<R> vv = xadd(v, xcross(w, xsub(wp, x)));
-      return rmin(wp.z, xadd(xadd(wp.z, xmul(dt, vv.z)), xmul(dt2, accel)));
-    };
-    auto accept = [&](V3<R> wp) {
-      bool ok = true;
-#pragma unroll
-      for (int c = 0; c < 3; ++c)
-        if (c < n && double(xhypot(xsub(world[c].x, wp.x), xsub(world[c].y, wp.y))) < .005) ok = false;
-      return ok;
-    };
     if (count <= 8) {
       V3<R> wps[8];
       R zs[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        if (k < count) zs[k] = point(k, wps[k]);
+        if (k < count) zs[k] = pickPoint(s, k, x, v, w, q, dt, dt2, accel, wps[k]);
       for (int pick = 0; pick < 4; ++pick) {
         int best = -1;
         R lowest = R(INFINITY);
@@ -348,7 +351,7 @@ template <class R, int T> struct Solver {
         for (int k = 0; k < 8; ++k) {
           if (k >= count) continue;
           const R z = zs[k];
-          if (double(z) >= .003 || z >= lowest || !accept(wps[k])) continue;
+          if (double(z) >= .003 || z >= lowest || !pickApart(wps[k], world, n)) continue;
           best = k;
           lowest = z;
           bestWorld = wps[k];
@@ -367,8 +370,8 @@ template <class R, int T> struct Solver {
       V3<R> bestWorld{};
       for (int k = 0; k < count; ++k) {
         V3<R> wp;
-        const R z = point(k, wp);
-        if (double(z) >= .003 || z >= lowest || !accept(wp)) continue;
+        const R z = pickPoint(s, k, x, v, w, q, dt, dt2, accel, wp);
+        if (double(z) >= .003 || z >= lowest || !pickApart(wp, world, n)) continue;
         best = k;
         lowest = z;
         bestWorld = wp;
@@ -424,7 +427,7 @@ template <class R, int T> struct Solver {
   // Warm-start key of a ground contact: shape and feature (point index).
   static __device__ __forceinline__ int groundKey(int shape, int feature) { return shape << 20 | feature; }
 
-  __device__ void detectContacts() {
+  __device__ __forceinline__ void detectContacts() {
     const int nb = m->nb;
     for (int b = team.lane; b < nb; b += T) I[L.colors + b] = ldg(m->color[b]);
     if (team.lane == 0) I[iColors] = 2;
@@ -730,12 +733,54 @@ template <class R, int T> struct Solver {
     stampAngular(H, g, e.axis * (-s), force, stiff);
   }
 
+  // Rows of contact ci acting on body bi (kernel.cuh:915-927): ground
+  // contacts are unit-axis linear rows at lever ra; body pairs are dense rows
+  // in the contact basis.  A member function (not a lambda) so that H and g
+  // stay in registers.
+  __device__ __forceinline__ void stampContact(int bi, int ci, V3<R> x, SV Rb, int nGround, R *H, R *g) const {
+    const R alpha = m->alpha;
+    const int meta = cmeta(ci);
+    const int body = metaBody(meta), other = metaOther(meta);
+    const SV c = contact(ci);
+    V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
+    if (other < 0) {
+      V3<R> ra = matVec(Rb, local);
+      V3<R> C = x + ra - V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]};
+      C.z -= alpha * c[cC0];
+      V3<R> f = coneForce(C, c);
+      if (f.z < R(0)) {
+        stampLinear(H, g, 0, ra, f.x, c[cPenalty]);
+        stampLinear(H, g, 1, ra, f.y, c[cPenalty + 1]);
+        stampLinear(H, g, 2, ra, f.z, c[cPenalty + 2]);
+        geometric(H, ra, f);
+      }
+    } else {
+      const SV bs = S + (L.CB + 9 * (ci - nGround));
+      V3<R> t1{bs[0], bs[1], bs[2]}, t2{bs[3], bs[4], bs[5]}, nn{bs[6], bs[7], bs[8]};
+      V3<R> ra = matVec(rot(body), local), rb = matVec(rot(other), V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]});
+      V3<R> delta = ld3(L.X + 3 * body) + ra - ld3(L.X + 3 * other) - rb;
+      V3<R> C{dot(delta, t1), dot(delta, t2), dot(delta, nn)};
+      C.z -= alpha * c[cC0];
+      const bool isOther = bi == other;
+      const R sign = isOther ? R(-1) : R(1);
+      const V3<R> r = isOther ? rb : ra;
+      V3<R> f = coneForce(C, c);
+      if (f.z < R(0)) {
+        V3<R> e0 = t1 * sign, e1 = t2 * sign, e2 = nn * sign;
+        stampDense(H, g, e0, cross(r, e0), f.x, c[cPenalty]);
+        stampDense(H, g, e1, cross(r, e1), f.y, c[cPenalty + 1]);
+        stampDense(H, g, e2, cross(r, e2), f.z, c[cPenalty + 2]);
+        geometric(H, r, (t1 * f.x + t2 * f.y + nn * f.z) * sign);
+      }
+    }
+  }
+
   // Block update of body bi (kernel.cuh:828-936).
   // With kSplit = 2 the two lanes of a pair (part 0 and 1) take alternate
   // items -- the inertia block, then each hinge, then each contact -- and
   // add their partial H and g with one shuffle per entry; both then solve
   // the same system and part 0 writes the pose.
-  __device__ R updateBody(int bi, R kp, R limit, int part = 0) {
+  __device__ __forceinline__ R updateBody(int bi, R kp, R limit, int part = 0) {
     const R h = m->dt, alpha = m->alpha;
     int item = 0;
     auto mine = [&]() { return kSplit == 1 || (item++ & 1) == part; };
@@ -812,55 +857,18 @@ template <class R, int T> struct Solver {
     // Contacts touching bi, in list order.
     const int nGround = I[iGround];
     const SV Rb = rot(bi);
-    auto touch = [&](int ci) {
-      if (!mine()) return;
-      const int meta = cmeta(ci);
-      const int body = metaBody(meta), other = metaOther(meta);
-      const SV c = contact(ci);
-      V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
-      if (other < 0) {
-        V3<R> ra = matVec(Rb, local);
-        V3<R> C = x + ra - V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]};
-        C.z -= alpha * c[cC0];
-        V3<R> f = coneForce(C, c);
-        if (f.z < R(0)) {
-          stampLinear(H, g, 0, ra, f.x, c[cPenalty]);
-          stampLinear(H, g, 1, ra, f.y, c[cPenalty + 1]);
-          stampLinear(H, g, 2, ra, f.z, c[cPenalty + 2]);
-          geometric(H, ra, f);
-        }
-      } else {
-        const SV bs = S + (L.CB + 9 * (ci - nGround));
-        V3<R> t1{bs[0], bs[1], bs[2]}, t2{bs[3], bs[4], bs[5]}, nn{bs[6], bs[7], bs[8]};
-        V3<R> ra = matVec(rot(body), local), rb = matVec(rot(other), V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]});
-        V3<R> delta = ld3(L.X + 3 * body) + ra - ld3(L.X + 3 * other) - rb;
-        V3<R> C{dot(delta, t1), dot(delta, t2), dot(delta, nn)};
-        C.z -= alpha * c[cC0];
-        const bool isOther = bi == other;
-        const R sign = isOther ? R(-1) : R(1);
-        const V3<R> r = isOther ? rb : ra;
-        V3<R> f = coneForce(C, c);
-        if (f.z < R(0)) {
-          V3<R> e0 = t1 * sign, e1 = t2 * sign, e2 = nn * sign;
-          stampDense(H, g, e0, cross(r, e0), f.x, c[cPenalty]);
-          stampDense(H, g, e1, cross(r, e1), f.y, c[cPenalty + 1]);
-          stampDense(H, g, e2, cross(r, e2), f.z, c[cPenalty + 2]);
-          geometric(H, r, (t1 * f.x + t2 * f.y + nn * f.z) * sign);
-        }
-      }
-    };
     if (L.cap <= 64) {
       unsigned long long mask = unsigned(I[L.masks + 2 * bi]) | (unsigned long long)unsigned(I[L.masks + 2 * bi + 1]) << 32;
       while (mask) {
         const int ci = __ffsll((long long)mask) - 1;
         mask &= mask - 1;
-        touch(ci);
+        if (mine()) stampContact(bi, ci, x, Rb, nGround, H, g);
       }
     } else {
       const int n = I[iCount];
       for (int ci = 0; ci < n; ++ci) {
         const int meta = cmeta(ci);
-        if (metaBody(meta) == bi || metaOther(meta) == bi) touch(ci);
+        if ((metaBody(meta) == bi || metaOther(meta) == bi) && mine()) stampContact(bi, ci, x, Rb, nGround, H, g);
       }
     }
     if constexpr (kSplit == 2) {
@@ -940,7 +948,7 @@ template <class R, int T> struct Solver {
     bool converged;
   };
 
-  __device__ bool step(Diag &diag, R kp, R limit) {
+  __device__ __forceinline__ bool step(Diag &diag, R kp, R limit) {
     const R h = m->dt, alpha = m->alpha, gamma = m->gamma;
     diag = {R(0), R(0), R(0), 0, 0, false};
     detectContacts();
@@ -1113,7 +1121,7 @@ template <class R, int T> struct Solver {
   }
 
   // BasicState::advance (kernel.cuh:421-443).
-  __device__ void advance(int substeps, R kp, R limit, Diag &summary) {
+  __device__ __forceinline__ void advance(int substeps, R kp, R limit, Diag &summary) {
     summary = {R(0), R(0), R(0), 0, 0, true};
     const R h = m->dt;
     if (!(h > R(0)) || m->iterations < 1) {
