@@ -172,7 +172,15 @@ __device__ __forceinline__ Hit xconvexContact(int sa, int sb, R inflation, R tol
 
 // Self-contact generation and warm start (kernel.cuh:654-722); returns the
 // new contact count.  Contacts follow the ground contacts in pair order.
-__device__ __forceinline__ int detectPairs(int base, int prevCount) {
+// Body-pair contacts run out of line on a by-value copy of the solver: the
+// caller's solver object never has its address taken, so it stays in
+// registers, and the narrow-phase code stays out of the hot instruction
+// stream.
+__device__ __forceinline__ int detectPairs(int base, int prevCount) { return pairPass(*this, base, prevCount); }
+static __device__ __noinline__ int pairPass(Solver self, int base, int prevCount) {
+  return self.detectPairsBody(base, prevCount);
+}
+__device__ __forceinline__ int detectPairsBody(int base, int prevCount) {
   const R dt = m->dt;
   const R tolerance = rmax(R(1e-8), xmul(m->tolerance, R(.1)));
   const R ag = xmul(m->alpha, m->gamma);

@@ -831,28 +831,16 @@ template <class R, int T> struct Solver {
           H[tri(3 + k, 3 + l)] = (J[0][k] * N[0][l] + J[1][k] * N[1][l] + J[2][k] * N[2][l]) * ih2;
       }
     }
-    // Hinges touching bi, in CSR order.  Without a split, two hinges are
-    // evaluated side by side: their geometry chains (rotations, atan2) are
-    // independent, which gives the scheduler two streams to interleave.
+    // Hinges touching bi, in CSR order.  One inlined copy of the hinge rows:
+    // the Gauss-Seidel loop is instruction-fetch bound, so its code is kept
+    // small rather than unrolled over hinge pairs.
     const int adjBegin = ldg(m->csrOffset[bi]), adjEnd = ldg(m->csrOffset[bi + 1]);
-    if constexpr (kSplit == 1) {
-      for (int adj = adjBegin; adj < adjEnd; adj += 2) {
-        const bool two = adj + 1 < adjEnd;
-        const int j0 = ldg(m->csrJoint[adj]), j1 = ldg(m->csrJoint[two ? adj + 1 : adj]);
-        JointGeo e0, e1;
-        evalJoint(j0, e0);
-        evalJoint(j1, e1);
-        stampHinge(bi, j0, e0, H, g, kp, limit);
-        if (two) stampHinge(bi, j1, e1, H, g, kp, limit);
-      }
-    } else {
-      for (int adj = adjBegin; adj < adjEnd; ++adj) {
-        if (!mine()) continue;
-        const int j = ldg(m->csrJoint[adj]);
-        JointGeo e;
-        evalJoint(j, e);
-        stampHinge(bi, j, e, H, g, kp, limit);
-      }
+    for (int adj = adjBegin; adj < adjEnd; ++adj) {
+      if (!mine()) continue;
+      const int j = ldg(m->csrJoint[adj]);
+      JointGeo e;
+      evalJoint(j, e);
+      stampHinge(bi, j, e, H, g, kp, limit);
     }
     // Contacts touching bi, in list order.
     const int nGround = I[iGround];
@@ -1040,15 +1028,11 @@ template <class R, int T> struct Solver {
       }
       maxUpdate = team.max(maxUpdate);
       R error = R(0);
-      // Joint multipliers, penalties and dry friction (kernel.cuh:991-1028),
-      // two hinges per lane evaluated side by side.
-      for (int j = team.lane; j < nj; j += 2 * T) {
-        const bool two = j + T < nj;
-        JointGeo e0, e1;
-        evalJoint(j, e0);
-        evalJoint(two ? j + T : j, e1);
-        dualHinge(j, e0, error);
-        if (two) dualHinge(j + T, e1, error);
+      // Joint multipliers, penalties and dry friction (kernel.cuh:991-1028).
+      for (int j = team.lane; j < nj; j += T) {
+        JointGeo e;
+        evalJoint(j, e);
+        dualHinge(j, e, error);
       }
       // Contact multipliers, stick flags and penalties (kernel.cuh:1029-1052).
       const int n = I[iCount], nGround = I[iGround];
