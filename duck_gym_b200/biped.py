@@ -354,6 +354,37 @@ def write_bam(directory, seed: int = 0, self_contacts: bool = False, **kwargs):
     return directory
 
 
+def with_parameters(text: str, mass=None, inertia=None, friction=None) -> str:
+    """The model text with one environment's physical parameters substituted:
+    body masses [B], principal inertias [B,3] and shape frictions [S] (None
+    keeps the model's).  Values are written with 17 significant digits, so a
+    float32 value read back is the same float32 -- this is how the per-env
+    parameters of ``CudaBatch.set_parameters`` are restated as model files for
+    the CPU oracle."""
+    lines = text.splitlines()
+    head = lines[0].split()
+    nb, nj, ns = int(head[2]), int(head[3]), int(head[4])
+
+    def fmt(v):
+        return format(float(v), ".17g")
+
+    for b in range(nb):
+        row = lines[2 + b].split()
+        if float(row[1]) > 0:
+            if mass is not None:
+                row[1] = fmt(mass[b])
+            if inertia is not None:
+                row[2:5] = [fmt(v) for v in inertia[b]]
+        lines[2 + b] = " ".join(row)
+    for k in range(ns):
+        at = 2 + nb + nj + k
+        row = lines[at].split()
+        if friction is not None:
+            row[12] = fmt(friction[k])
+        lines[at] = " ".join(row)
+    return "\n".join(lines) + "\n"
+
+
 def write(directory, seed: int = 0, self_contacts: bool = False, name: str = "microduck.duck"):
     """Write ``<directory>/<name>`` and ``metadata.json``; return the model path."""
     directory = Path(directory)

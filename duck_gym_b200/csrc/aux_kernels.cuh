@@ -199,7 +199,7 @@ __device__ __forceinline__ V3<R> envGroundForce(const DevModel<R> *m, const R *r
 // applied actuator) per hinge.
 template <class R>
 __device__ __noinline__ void envGeneralizedLoads(const DevModel<R> *__restrict__ m, const R *rec, V3<R> off,
-                                                 R *o) {
+                                                 R *o, const R *envMass = nullptr, const R *envInertia = nullptr) {
   const int nb = m->nb, nj = m->nj;
   const R *bodies = rec + kRecHeader;
   const R *joints = bodies + kRecBody * nb;
@@ -220,8 +220,11 @@ __device__ __noinline__ void envGeneralizedLoads(const DevModel<R> *__restrict__
   }
   const V3<R> gravity{m->gravity[0], m->gravity[1], m->gravity[2]};
   for (int i = 1; i < nb; ++i) {
-    const R mass = __ldg(&m->mass[i]);
-    const V3<R> in = mvec(m->inertia[i]);
+    const R modelMass = __ldg(&m->mass[i]);
+    const bool dynamic = modelMass > R(0);
+    const R mass = envMass && dynamic ? envMass[i] : modelMass;
+    const V3<R> in = envInertia && dynamic ? V3<R>{envInertia[3 * i], envInertia[3 * i + 1], envInertia[3 * i + 2]}
+                                           : mvec(m->inertia[i]);
     const Q4<R> q = Q(i);
     auto inertiaMul = [&](V3<R> v) {
       V3<R> l = rotateInv(q, v);
@@ -265,11 +268,42 @@ __device__ __noinline__ void envGeneralizedLoads(const DevModel<R> *__restrict__
 // BasicState::generalizedLoads (kernel.cuh:504-554), one thread per environment.
 template <class R>
 __global__ void generalizedLoadsKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
-                                       const R *offset, R *out) {
+                                       const R *offset, R *out, const R *envMass, const R *envInertia) {
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= count) return;
   const R *off = offset + 3 * size_t(e);
-  envGeneralizedLoads(m, records + size_t(e) * stride, V3<R>{off[0], off[1], off[2]}, out + size_t(e) * m->nj * 3);
+  envGeneralizedLoads(m, records + size_t(e) * stride, V3<R>{off[0], off[1], off[2]}, out + size_t(e) * m->nj * 3,
+                      envMass ? envMass + size_t(e) * m->nb : nullptr,
+                      envInertia ? envInertia + size_t(e) * m->nb * 3 : nullptr);
+}
+
+// Per-environment parameter check: a non-finite or non-positive mass or
+// inertia of a dynamic body, or a negative or non-finite friction, marks the
+// environment failed (the sticky diag[:, 5] flag) instead of raising.
+template <class R>
+__global__ void checkParametersKernel(const DevModel<R> *__restrict__ m, R *records, int stride, int count,
+                                      const R *envMass, const R *envInertia, const R *envFriction) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= count) return;
+  bool bad = false;
+  for (int b = 0; b < m->nb; ++b) {
+    if (!(__ldg(&m->mass[b]) > R(0))) continue;
+    if (envMass) {
+      const R v = envMass[size_t(e) * m->nb + b];
+      bad |= !(v > R(0)) || !isfinite(v);
+    }
+    if (envInertia)
+      for (int k = 0; k < 3; ++k) {
+        const R v = envInertia[(size_t(e) * m->nb + b) * 3 + k];
+        bad |= !(v > R(0)) || !isfinite(v);
+      }
+  }
+  if (envFriction)
+    for (int s = 0; s < m->ns; ++s) {
+      const R v = envFriction[size_t(e) * m->ns + s];
+      bad |= !(v >= R(0)) || !isfinite(v);
+    }
+  if (bad) records[size_t(e) * stride] = R(1);
 }
 
 // Validation of the generalized-load offsets happens on the device: a

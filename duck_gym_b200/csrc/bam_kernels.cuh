@@ -61,6 +61,7 @@ template <class R> struct BamBuffers {
   long long *episodeLength;
   int *counters;  // [0] delay-ring cursor, [1] common step counter
   float *obsActor, *obsCritic, *reward;
+  const R *envMass = nullptr, *envInertia = nullptr;  // the batch's randomised parameters, if any
 };
 
 // torch.lerp on the CPU: start + w (end - start) below w = 0.5, else
@@ -105,7 +106,8 @@ __global__ void bamServoKernel(const DevModel<R> *__restrict__ m, const R *recor
   const bool init = B.histInit[e];
   R loads[3 * kMaxJoints];
   const R *off = B.rootOffset + 3 * size_t(e);
-  envGeneralizedLoads(m, rec, V3<R>{off[0], off[1], off[2]}, loads);
+  envGeneralizedLoads(m, rec, V3<R>{off[0], off[1], off[2]}, loads, B.envMass ? B.envMass + size_t(e) * m->nb : nullptr,
+                      B.envInertia ? B.envInertia + size_t(e) * m->nb * 3 : nullptr);
   R sumAbs = R(0);
   for (int j = 0; j < nj; ++j) sumAbs += fabs(B.prevMotor[size_t(e) * nj + j]);
   const R supply = rmax(R(p.vin) - R(p.vinDrop) * sumAbs, R(p.vinMin));

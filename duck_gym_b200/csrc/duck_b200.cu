@@ -49,6 +49,8 @@ struct duck_batch {
   int T = 8, teamsPerBlock = 4, smemPerBlock = 0;
   Layout layout{};
   void *devModel = nullptr, *points = nullptr, *records = nullptr;
+  // Per-environment parameters (duck_batch_set_parameters), nullptr = model's.
+  void *envMass = nullptr, *envInertia = nullptr, *envFriction = nullptr;
   size_t modelBytes = 0;
   cudaEvent_t ready = nullptr;
   std::vector<std::string> names;
@@ -102,7 +104,11 @@ template <class R> void setupAdvance(duck_batch *b) {
   }
 }
 
-template <class R> void launchAdvance(duck_batch *b, const StepArgs &args, cudaStream_t s) {
+template <class R> void launchAdvance(duck_batch *b, const StepArgs &stepArgs, cudaStream_t s) {
+  StepArgs args = stepArgs;
+  args.mass = b->envMass;
+  args.inertia = b->envInertia;
+  args.friction = b->envFriction;
   const int grid = blocksFor(b->n, b->teamsPerBlock);
   const R *pts = static_cast<const R *>(b->points);
   const DevModel<R> *m = static_cast<const DevModel<R> *>(b->devModel);
@@ -125,8 +131,8 @@ template <class R> void launchReset(duck_batch *b, const uint8_t *mask, const vo
 }
 
 template <class R> duck_batch *create(const ParsedModel &parsed, int n, double dt, int iterations, int device,
-                                      bool specialized, cudaStream_t s) {
-  auto hm = std::make_shared<HostModel<R>>(convertModel<R>(parsed, dt, iterations, specialized));
+                                      bool specialized, int maxPairs, cudaStream_t s) {
+  auto hm = std::make_shared<HostModel<R>>(convertModel<R>(parsed, dt, iterations, specialized, maxPairs));
   auto b = std::make_unique<duck_batch>();
   b->device = device;
   b->fp64 = std::is_same_v<R, double>;
@@ -205,7 +211,8 @@ template <class R> void statsLaunch(duck_batch *b, void *counts, void *self, cud
 template <class R> void loadsLaunch(duck_batch *b, const void *offset, void *out, cudaStream_t s) {
   generalizedLoadsKernel<R><<<blocksFor(b->n, 64), 64, 0, s>>>(
       static_cast<const DevModel<R> *>(b->devModel), static_cast<const R *>(b->records), b->recordStride, b->n,
-      static_cast<const R *>(offset), static_cast<R *>(out));
+      static_cast<const R *>(offset), static_cast<R *>(out), static_cast<const R *>(b->envMass),
+      static_cast<const R *>(b->envInertia));
   ++b->launches;
 }
 }  // namespace
@@ -214,20 +221,29 @@ extern "C" {
 
 const char *duck_last_error(void) { return lastError.c_str(); }
 
-int duck_batch_create(const char *model_path, int num_envs, double dt, int iterations, int device, int fp64,
-                      int specialized, int shared_memory, duck_stream stream, duck_batch **out) {
+int duck_batch_create_ex(const char *model_path, int num_envs, double dt, int iterations, int device, int fp64,
+                         int specialized, int shared_memory, const duck_batch_options *options, duck_stream stream,
+                         duck_batch **out) {
   return guarded([&] {
     require(out != nullptr && model_path != nullptr, "Invalid arguments");
     *out = nullptr;
     require(specialized || !shared_memory, "Shared memory requires the compact MicroDuck backend");
     require(num_envs > 0 && num_envs <= 65536 && dt > 0 && std::isfinite(dt) && iterations > 0,
             "Invalid batch parameters");
+    const int maxPairs = options ? options->max_pairs : kReferencePairs;
+    require(maxPairs >= 0 && maxPairs <= kMaxPairs, "max_pairs must be in [0, 128]");
     DeviceGuard guard(device);
-    ParsedModel parsed = parseDuck(model_path);
+    ParsedModel parsed = parseDuck(model_path, maxPairs);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    *out = fp64 ? create<double>(parsed, num_envs, dt, iterations, device, specialized, s)
-                : create<float>(parsed, num_envs, dt, iterations, device, specialized, s);
+    *out = fp64 ? create<double>(parsed, num_envs, dt, iterations, device, specialized, maxPairs, s)
+                : create<float>(parsed, num_envs, dt, iterations, device, specialized, maxPairs, s);
   });
+}
+
+int duck_batch_create(const char *model_path, int num_envs, double dt, int iterations, int device, int fp64,
+                      int specialized, int shared_memory, duck_stream stream, duck_batch **out) {
+  return duck_batch_create_ex(model_path, num_envs, dt, iterations, device, fp64, specialized, shared_memory, nullptr,
+                              stream, out);
 }
 
 void duck_batch_destroy(duck_batch *b) {
@@ -240,6 +256,9 @@ void duck_batch_destroy(duck_batch *b) {
   cudaFree(b->devModel);
   cudaFree(b->points);
   cudaFree(b->records);
+  cudaFree(b->envMass);
+  cudaFree(b->envInertia);
+  cudaFree(b->envFriction);
   delete b;
 }
 
@@ -248,6 +267,16 @@ int duck_batch_info(const duck_batch *b, int32_t *out) {
     require(b && out, "Invalid arguments");
     int32_t v[10] = {b->n, b->nb, b->nj, b->bound, b->recordLength, b->fp64, b->device, b->teamsPerBlock, b->T,
                      b->smemPerBlock};
+    std::memcpy(out, v, sizeof(v));
+  });
+}
+
+int duck_batch_model_counts(const duck_batch *b, int32_t *out) {
+  return guarded([&] {
+    require(b && out, "Invalid arguments");
+    const int ns = b->fp64 ? host<double>(b).dev.ns : host<float>(b).dev.ns;
+    const int np = b->fp64 ? host<double>(b).dev.np : host<float>(b).dev.np;
+    const int32_t v[4] = {b->nb, b->nj, ns, np};
     std::memcpy(out, v, sizeof(v));
   });
 }
@@ -768,7 +797,9 @@ enum BamPart { kBamBegin = 1, kBamSubstep = 2, kBamFinish = 4, kBamServoOnly = 8
 template <class R>
 void bamRun(duck_batch *b, const BamKernelParams &k, const duck_bam_buffers *x, const void *actions, int parts,
             int substeps, cudaStream_t s) {
-  const BamBuffers<R> B = bamBuffers<R>(x);
+  BamBuffers<R> B = bamBuffers<R>(x);
+  B.envMass = static_cast<const R *>(b->envMass);
+  B.envInertia = static_cast<const R *>(b->envInertia);
   const DevModel<R> *m = static_cast<const DevModel<R> *>(b->devModel);
   const R *rec = static_cast<const R *>(b->records);
   const int grid = blocksFor(b->n, 128);
@@ -874,6 +905,43 @@ int duck_bam_observe(duck_batch *b, const duck_bam_params *p, const duck_bam_buf
       bamControlKernel<R><<<blocksFor(b->n, 128), 128, 0, s>>>(
           static_cast<const DevModel<R> *>(b->devModel), static_cast<const R *>(b->records), b->recordStride, b->n,
           k, bamBuffers<R>(x), update_heading ? 1 : 2, reinterpret_cast<const bool *>(mask));
+    };
+    if (b->fp64) run(0.0); else run(0.0f);
+    ++b->launches;
+    finish(b, s);
+  });
+}
+
+int duck_batch_set_parameters(duck_batch *b, const void *mass, const void *inertia, const void *friction,
+                              duck_stream stream) {
+  return guarded([&] {
+    require(b != nullptr, "Invalid arguments");
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const size_t real = b->fp64 ? 8 : 4;
+    const int ns = b->fp64 ? host<double>(b).dev.ns : host<float>(b).dev.ns;
+    begin(b, s);
+    auto install = [&](void *&slot, const void *src, size_t count, const char *what) {
+      if (!src) {
+        if (slot) {
+          check(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+          check(cudaFree(slot), "cudaFree");
+          slot = nullptr;
+        }
+        return;
+      }
+      if (!slot) check(cudaMalloc(&slot, count * real), what);
+      check(cudaMemcpyAsync(slot, src, count * real, cudaMemcpyDeviceToDevice, s), what);
+    };
+    install(b->envMass, mass, size_t(b->n) * b->nb, "per-env masses");
+    install(b->envInertia, inertia, size_t(b->n) * b->nb * 3, "per-env inertias");
+    install(b->envFriction, friction, size_t(b->n) * ns, "per-env frictions");
+    auto run = [&](auto zero) {
+      using R = decltype(zero);
+      checkParametersKernel<R><<<blocksFor(b->n, 128), 128, 0, s>>>(
+          static_cast<const DevModel<R> *>(b->devModel), static_cast<R *>(b->records), b->recordStride, b->n,
+          static_cast<const R *>(b->envMass), static_cast<const R *>(b->envInertia),
+          static_cast<const R *>(b->envFriction));
     };
     if (b->fp64) run(0.0); else run(0.0f);
     ++b->launches;

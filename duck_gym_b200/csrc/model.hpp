@@ -19,7 +19,11 @@
 
 namespace duckb200 {
 
-constexpr int kMaxBodies = 32, kMaxJoints = 32, kMaxShapes = 32, kMaxPairs = 32;
+// The reference caps body-collision pairs at 32 (solver.cpp:151-152,
+// model.hpp:26-29); kReferencePairs keeps that limit by default.  Batches
+// created with a larger pair limit (up to kMaxPairs) accept models with more
+// pairs -- an extension beyond the reference.
+constexpr int kMaxBodies = 32, kMaxJoints = 32, kMaxShapes = 32, kMaxPairs = 128, kReferencePairs = 32;
 
 template <class R> struct DevModel {
   int nb, nj, ns, np;
@@ -97,7 +101,7 @@ struct ParsedModel {
   std::vector<Pair> pairs;
 };
 
-inline ParsedModel parseDuck(const std::string &path) {
+inline ParsedModel parseDuck(const std::string &path, int maxPairs = kReferencePairs) {
   std::ifstream in(path);
   if (!in) throw std::runtime_error("Cannot read model: " + path);
   auto unitOf = [](DVec a) {
@@ -169,7 +173,7 @@ inline ParsedModel parseDuck(const std::string &path) {
   if (version == 2) {
     int count = -1;
     in >> count;
-    if (count < 0 || count > 32) throw std::runtime_error("Invalid body collision pair count");
+    if (count < 0 || count > maxPairs) throw std::runtime_error("Invalid body collision pair count");
     for (int k = 0; k < count; ++k) {
       ParsedModel::Pair p;
       in >> p.a >> p.b >> p.friction;
@@ -194,9 +198,11 @@ template <class R> struct HostModel {
 };
 
 template <class R>
-HostModel<R> convertModel(const ParsedModel &o, double dt, int iterations, bool specialized) {
+HostModel<R> convertModel(const ParsedModel &o, double dt, int iterations, bool specialized,
+                          int maxPairs = kReferencePairs) {
   auto require = [](bool c, const char *msg) { if (!c) throw std::invalid_argument(msg); };
-  require(o.bodies.size() <= 32 && o.joints.size() <= 32 && o.shapes.size() <= 32 && o.pairs.size() <= 32,
+  require(o.bodies.size() <= 32 && o.joints.size() <= 32 && o.shapes.size() <= 32 &&
+              int(o.pairs.size()) <= std::min(maxPairs, kMaxPairs),
           "CUDA model capacity exceeded (32 bodies/joints/shapes)");
   require(o.bodies.size() > 1, "CUDA batch needs at least one body");
   const int contactCapacity = specialized ? 64 : 160;

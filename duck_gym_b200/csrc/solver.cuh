@@ -132,6 +132,10 @@ struct StepArgs {
   const void *motor;    // [E,J,3] (step_motor) or nullptr
   int substeps;
   double kp, limit;
+  // Per-environment physical parameters (domain randomisation, an extension
+  // beyond the reference's shared model), nullptr = the model's values:
+  // body masses [E,B], principal inertias [E,B,3], shape frictions [E,S].
+  const void *mass = nullptr, *inertia = nullptr, *friction = nullptr;
 };
 
 template <class R, int T> struct Solver {
@@ -149,6 +153,8 @@ template <class R, int T> struct Solver {
   R *rec;                  // environment's global record
   const Layout &L;
   Team<T> team;
+  // This environment's randomised parameters (nullptr: the model's).
+  const R *envMass = nullptr, *envInertia = nullptr, *envFriction = nullptr;
 
   __device__ Solver(const DevModel<R> *model, const R *points, R *smemTeam, R *record, const Layout &layout)
       : m(model), pts(points), S{smemTeam}, rec(record), L(layout) {
@@ -172,6 +178,17 @@ template <class R, int T> struct Solver {
 #pragma unroll
     for (int k = 0; k < 9; ++k) S[L.RM + 9 * b + k] = mm[k];
   }
+  // Mass, principal inertia and ground friction of this environment: the
+  // model's, or the randomised values for dynamic bodies.
+  __device__ __forceinline__ R massOf(int b) const {
+    const R mm = ldg(m->mass[b]);
+    return envMass && mm > R(0) ? envMass[b] : mm;
+  }
+  __device__ __forceinline__ V3<R> inertiaOf(int b) const {
+    return envInertia && ldg(m->mass[b]) > R(0) ? V3<R>{envInertia[3 * b], envInertia[3 * b + 1], envInertia[3 * b + 2]}
+                                                : mv3(m->inertia[b]);
+  }
+  __device__ __forceinline__ R frictionOf(int s) const { return envFriction ? envFriction[s] : ldg(m->sFriction[s]); }
   // Velocities live in the XQP slots between substeps (predicted poses inside).
   __device__ __forceinline__ V3<R> vel(int b) const { return ld3(L.XQP + 7 * b); }
   __device__ __forceinline__ V3<R> omega(int b) const { return ld3(L.XQP + 7 * b + 3); }
@@ -321,7 +338,7 @@ template <class R, int T> struct Solver {
   // predicted below 3 mm (kernel.cuh:338-364, 601-653), on one lane.
   __device__ __forceinline__ int groundPicks(int s, int *feature, V3<R> *world) const {
     const int b = ldg(m->sBody[s]);
-    const R mass = ldg(m->mass[b]);
+    const R mass = massOf(b);
     if (!m->ground || !ldg(m->sGround[s]) || mass == R(0)) return 0;
     const R dt = m->dt;
     V3<R> x = ld3(L.X + 3 * b), v = vel(b), w = omega(b);
@@ -413,7 +430,7 @@ template <class R, int T> struct Solver {
     cfeat(slot) = best;
     c[cLocal] = local.x; c[cLocal + 1] = local.y; c[cLocal + 2] = local.z;
     c[cAnchor] = anchor.x; c[cAnchor + 1] = anchor.y; c[cAnchor + 2] = anchor.z;
-    c[cFriction] = ldg(m->sFriction[s]);
+    c[cFriction] = frictionOf(s);
     c[cC0] = c0;
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
@@ -785,7 +802,7 @@ template <class R, int T> struct Solver {
     int item = 0;
     auto mine = [&]() { return kSplit == 1 || (item++ & 1) == part; };
     const R ih = R(1) / h, ih2 = ih * ih;
-    const R mass = ldg(m->mass[bi]);
+    const R mass = massOf(bi);
     R H[21], g[6];
 #pragma unroll
     for (int i = 0; i < 21; ++i) H[i] = R(0);
@@ -978,9 +995,9 @@ template <class R, int T> struct Solver {
       const Q4<R> q = quat(b);
       x0r[k] = x;
       q0r[k] = q;
-      const R mass = ldg(m->mass[b]);
+      const R mass = massOf(b);
       if (mass == R(0)) continue;
-      V3<R> in = mv3(m->inertia[b]);
+      V3<R> in = inertiaOf(b);
       // World inertia R diag(I) R^T at q0 (kept for the whole substep).
       const SV Rm = rot(b);
       V3<R> ex{Rm[0], Rm[3], Rm[6]}, ey{Rm[1], Rm[4], Rm[7]}, ez{Rm[2], Rm[5], Rm[8]};
@@ -1147,6 +1164,9 @@ __global__ void __launch_bounds__(32, T >= 16 ? 14 : 1) advanceKernel(const DevM
   R *teamBase = reinterpret_cast<R *>(smemRaw) + team;
   R *rec = records + size_t(env) * recordStride;
   Solver<R, T> s(model, points, teamBase, rec, L);
+  if (args.mass) s.envMass = static_cast<const R *>(args.mass) + size_t(env) * model->nb;
+  if (args.inertia) s.envInertia = static_cast<const R *>(args.inertia) + size_t(env) * model->nb * 3;
+  if (args.friction) s.envFriction = static_cast<const R *>(args.friction) + size_t(env) * model->ns;
   const typename Solver<R, T>::SV S = s.S;
   const int nj = model->nj;
   const int lane = s.team.lane;

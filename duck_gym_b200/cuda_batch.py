@@ -49,6 +49,7 @@ def library():
         P, I, D = ctypes.c_void_p, ctypes.c_int, ctypes.c_double
         lib.duck_last_error.restype = ctypes.c_char_p
         lib.duck_batch_create.argtypes = [ctypes.c_char_p, I, D, I, I, I, I, I, P, ctypes.POINTER(P)]
+        lib.duck_batch_create_ex.argtypes = [ctypes.c_char_p, I, D, I, I, I, I, I, P, P, ctypes.POINTER(P)]
         lib.duck_batch_destroy.argtypes = [P]
         lib.duck_batch_destroy.restype = None
         lib.duck_batch_info.argtypes = [P, P]
@@ -66,6 +67,8 @@ def library():
         lib.duck_batch_export.argtypes = [P, I, I, P, P]
         lib.duck_batch_import.argtypes = [P, I, I, P, P]
         lib.duck_batch_contact_keys.argtypes = [P, I, P, I, ctypes.POINTER(I), P]
+        lib.duck_batch_set_parameters.argtypes = [P, P, P, P, P]
+        lib.duck_batch_model_counts.argtypes = [P, P]
         lib.duck_batch_launches.argtypes = [P]
         lib.duck_batch_launches.restype = ctypes.c_int64
         lib.duck_fp32_peak.argtypes = [I, I, ctypes.POINTER(D), P]
@@ -81,7 +84,8 @@ def library():
             getattr(lib, name).argtypes = [P, P, P, P]
         lib.duck_bam_reset_buffers.argtypes = [P, P, P, P, P]
         lib.duck_bam_observe.argtypes = [P, P, P, P, I, P]
-        for name in ("duck_batch_create", "duck_batch_info", "duck_batch_reset", "duck_batch_step",
+        for name in ("duck_batch_create", "duck_batch_create_ex", "duck_batch_set_parameters", "duck_batch_model_counts",
+                     "duck_batch_info", "duck_batch_reset", "duck_batch_step",
                      "duck_batch_step_motor", "duck_batch_state", "duck_batch_contact_forces",
                      "duck_batch_self_contact_stats", "duck_batch_contact_counts",
                      "duck_batch_generalized_loads", "duck_batch_reference", "duck_batch_export",
@@ -107,15 +111,19 @@ class CudaBatch:
     """Batched AVBD environments on one GPU (drop-in for ``_duck_cuda.CudaBatch``)."""
 
     def __init__(self, model, num_envs, dt=0.001, iterations=200, device=0, fp64=False,
-                 specialized=False, shared_memory=False):
+                 specialized=False, shared_memory=False, max_pairs=32):
+        """``max_pairs`` (extension): largest accepted number of body-collision
+        pairs; 32 is the reference's limit, up to 128 accepted."""
         lib = library()
         self.device = torch.device("cuda", int(device))
         handle = ctypes.c_void_p()
+        options = (ctypes.c_int * 1)(int(max_pairs))
         with torch.cuda.device(self.device):
-            status = lib.duck_batch_create(str(model).encode(), int(num_envs), float(dt),
-                                           int(iterations), int(device), int(bool(fp64)),
-                                           int(bool(specialized)), int(bool(shared_memory)),
-                                           _stream(self.device), ctypes.byref(handle))
+            status = lib.duck_batch_create_ex(str(model).encode(), int(num_envs), float(dt),
+                                              int(iterations), int(device), int(bool(fp64)),
+                                              int(bool(specialized)), int(bool(shared_memory)),
+                                              ctypes.cast(options, ctypes.c_void_p),
+                                              _stream(self.device), ctypes.byref(handle))
         _raise(status)
         self._h = handle.value
         info = (ctypes.c_int32 * 10)()
@@ -124,6 +132,9 @@ class CudaBatch:
          _, _, self.envs_per_block, self.lanes_per_env, self.shared_bytes_per_block) = list(info)
         self.dtype = torch.float64 if fp64 else torch.float32
         self._names = [lib.duck_batch_joint_name(self._h, i).decode() for i in range(self.num_joints)]
+        counts = (ctypes.c_int32 * 4)()
+        _raise(lib.duck_batch_model_counts(self._h, counts))
+        self.num_shapes, self.num_pairs = int(counts[2]), int(counts[3])
 
     def __del__(self):
         h = getattr(self, "_h", None)
@@ -249,6 +260,19 @@ class CudaBatch:
             _raise(library().duck_batch_contact_keys(self._h, int(env), keys.ctypes.data_as(ctypes.c_void_p),
                                                      cap, ctypes.byref(count), _stream(self.device)))
         return keys[:count.value].copy()
+
+    def set_parameters(self, mass=None, inertia=None, friction=None):
+        """Per-environment physical parameters (extension; the reference shares
+        one model): body masses [E,B], principal inertias [E,B,3], ground
+        friction per shape [E,S], CUDA tensors of the batch dtype; None keeps
+        or restores the model's values.  Invalid values set the environment's
+        failure flag."""
+        E, B = self.num_envs, self.num_bodies
+        with torch.cuda.device(self.device):
+            mp = self._check(mass, (E, B)) if mass is not None else None
+            ip = self._check(inertia, (E, B, 3)) if inertia is not None else None
+            fp = self._check(friction, (E, self.num_shapes)) if friction is not None else None
+            _raise(library().duck_batch_set_parameters(self._h, mp, ip, fp, _stream(self.device)))
 
     @property
     def launches(self):

@@ -48,6 +48,21 @@ const char *duck_last_error(void);
 int duck_batch_create(const char *model_path, int num_envs, double dt, int iterations, int device,
                       int fp64, int specialized, int shared_memory, duck_stream stream,
                       duck_batch **out);
+/* Options of duck_batch_create_ex (extensions beyond the reference). */
+typedef struct duck_batch_options {
+  /* Largest accepted number of body-collision pairs.  32 is the reference's
+   * limit (solver.cpp:151-152, model.hpp:26-29) and what duck_batch_create
+   * uses; up to 128 accepts models the reference rejects (for example all 91
+   * non-adjacent link pairs of the 15-link biped).  The contact bound
+   * (pairs + 4 per ground shape <= 160) still applies. */
+  int max_pairs;
+} duck_batch_options;
+
+/* duck_batch_create with options (NULL = the reference's limits). */
+int duck_batch_create_ex(const char *model_path, int num_envs, double dt, int iterations, int device,
+                         int fp64, int specialized, int shared_memory, const duck_batch_options *options,
+                         duck_stream stream, duck_batch **out);
+
 /* Replaces Batch::~Batch (extension.cu:266-272). */
 void duck_batch_destroy(duck_batch *batch);
 
@@ -55,6 +70,9 @@ void duck_batch_destroy(duck_batch *batch);
  * record length (Reals), out[5] fp64, out[6] device, out[7] environments per
  * CTA, out[8] lanes per environment, out[9] shared bytes per CTA. */
 int duck_batch_info(const duck_batch *batch, int32_t *out);
+/* No reference counterpart.  Model sizes: out[0] bodies, out[1] joints,
+ * out[2] collision shapes, out[3] body-collision pairs. */
+int duck_batch_model_counts(const duck_batch *batch, int32_t *out);
 /* Joint name i (the reference's joint_names property, extension.cu:416-421). */
 const char *duck_batch_joint_name(const duck_batch *batch, int index);
 
@@ -269,6 +287,19 @@ int duck_bam_reset_buffers(duck_batch *batch, const duck_bam_params *params,
  * when heading hold is on. */
 int duck_bam_observe(duck_batch *batch, const duck_bam_params *params, const duck_bam_buffers *buffers,
                      const uint8_t *mask, int update_heading, duck_stream stream);
+
+/* No reference counterpart (the reference shares one model across every
+ * environment, kernel.cuh:331): per-environment physical parameters for
+ * domain randomisation.  mass [E,B] body masses, inertia [E,B,3] principal
+ * inertias, friction [E,S] ground friction of each collision shape -- device
+ * arrays of Real, copied into the batch; NULL restores the model's values for
+ * that quantity.  Static bodies (model mass 0) stay static.  Values take effect
+ * from the next step: physics, generalized loads and the BAM servo use them.
+ * A non-finite or non-positive mass or inertia of a dynamic body, or a
+ * negative or non-finite friction, sets that environment's failure flag
+ * (diag[:, 5]).  Body-pair friction keeps the model's values. */
+int duck_batch_set_parameters(duck_batch *batch, const void *mass, const void *inertia,
+                              const void *friction, duck_stream stream);
 
 /* No reference counterpart.  Number of kernel launches issued by this batch
  * since creation (for launch accounting in benchmarks). */

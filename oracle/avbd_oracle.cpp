@@ -70,8 +70,8 @@ template <class F> void parallel(int n, int threads, F &&work) {
 template <class R> struct Batch final : BatchBase {
   Model<R> model;
   std::vector<Env<R, double>> envs;
-  Batch(const DModel &d, int count, double dt, int iterations, int capacity) {
-    model = convertModel<R>(d, dt, iterations, capacity);
+  Batch(const DModel &d, int count, double dt, int iterations, int capacity, int maxPairs = 32) {
+    model = convertModel<R>(d, dt, iterations, capacity, 32, 32, maxPairs);
     n = count;
     bodies = int(model.bodies.size());
     joints = int(model.joints.size());
@@ -258,17 +258,21 @@ BatchBase *B(void *p) { return static_cast<BatchBase *>(p); }
 extern "C" {
 const char *avbd_oracle_last_error() { return lastError.c_str(); }
 
-void *avbd_oracle_create(const char *path, int n, double dt, int iterations, int fp64, int capacity) {
+void *avbd_oracle_create_ex(const char *path, int n, double dt, int iterations, int fp64, int capacity,
+                            int maxPairs) {
   try {
-    if (!(n > 0 && n <= 65536 && dt > 0 && std::isfinite(dt) && iterations > 0))
+    if (!(n > 0 && n <= 65536 && dt > 0 && std::isfinite(dt) && iterations > 0 && maxPairs >= 0 && maxPairs <= 128))
       throw std::invalid_argument("Invalid batch parameters");
-    DModel d = loadDuck(path);
-    if (fp64) return new Batch<double>(d, n, dt, iterations, capacity);
-    return new Batch<float>(d, n, dt, iterations, capacity);
+    DModel d = loadDuck(path, maxPairs);
+    if (fp64) return new Batch<double>(d, n, dt, iterations, capacity, maxPairs);
+    return new Batch<float>(d, n, dt, iterations, capacity, maxPairs);
   } catch (const std::exception &e) {
     lastError = e.what();
     return nullptr;
   }
+}
+void *avbd_oracle_create(const char *path, int n, double dt, int iterations, int fp64, int capacity) {
+  return avbd_oracle_create_ex(path, n, dt, iterations, fp64, capacity, 32);
 }
 void avbd_oracle_destroy(void *b) { delete B(b); }
 int avbd_oracle_info(void *b, int32_t *out) {

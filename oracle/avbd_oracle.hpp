@@ -305,7 +305,10 @@ inline Q4<double> dnormalized(Q4<double> q) {
   return {q.w / n, q.x / n, q.y / n, q.z / n};
 }
 
-inline DModel loadDuck(const std::string &path) {
+// maxPairs: the reference rejects more than 32 body-collision pairs
+// (solver.cpp:151-152); larger limits restate the same algorithm with a raised
+// capacity, the checker of the library's pair-limit extension.
+inline DModel loadDuck(const std::string &path, int maxPairs = 32) {
   std::ifstream in(path);
   if (!in) throw std::runtime_error("Cannot read model: " + path);
   DModel m;
@@ -365,7 +368,7 @@ inline DModel loadDuck(const std::string &path) {
   if (version == 2) {
     int count = -1;
     in >> count;
-    if (count < 0 || count > 32) throw std::runtime_error("Invalid body collision pair count");
+    if (count < 0 || count > maxPairs) throw std::runtime_error("Invalid body collision pair count");
     for (int k = 0; k < count; ++k) {
       DModel::P p;
       in >> p.a >> p.b >> p.friction;
@@ -390,9 +393,10 @@ template <class R> Q4<R> toR(Q4<double> q) { return {R(q.w), R(q.x), R(q.y), R(q
 // the compact MicroDuck state (kernel.cuh:1097-1098).
 template <class R>
 Model<R> convertModel(const DModel &o, double dt, int iterations, int contactCapacity,
-                      int bodyCapacity = 32, int jointCapacity = 32) {
+                      int bodyCapacity = 32, int jointCapacity = 32, int maxPairs = 32) {
   auto require = [](bool c, const char *m) { if (!c) throw std::invalid_argument(m); };
-  require(o.bodies.size() <= 32 && o.joints.size() <= 32 && o.shapes.size() <= 32 && o.pairs.size() <= 32,
+  require(o.bodies.size() <= 32 && o.joints.size() <= 32 && o.shapes.size() <= 32 &&
+              int(o.pairs.size()) <= maxPairs,
           "CUDA model capacity exceeded (32 bodies/joints/shapes)");
   require(o.bodies.size() > 1, "CUDA batch needs at least one body");
   require(int(o.bodies.size()) <= bodyCapacity && int(o.joints.size()) <= jointCapacity,

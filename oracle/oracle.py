@@ -33,6 +33,8 @@ def library():
         lib.avbd_oracle_last_error.restype = ctypes.c_char_p
         lib.avbd_oracle_create.restype = P
         lib.avbd_oracle_create.argtypes = [ctypes.c_char_p, I, D, I, I, I]
+        lib.avbd_oracle_create_ex.restype = P
+        lib.avbd_oracle_create_ex.argtypes = [ctypes.c_char_p, I, D, I, I, I, I]
         lib.avbd_oracle_destroy.argtypes = [P]
         lib.avbd_oracle_info.argtypes = [P, P]
         for name, args in {
@@ -72,10 +74,10 @@ class OracleBatch:
     list size (160 for the reference's generic state, 64 for the compact one)."""
 
     def __init__(self, model, num_envs, dt, iterations, threads=1, fp64=False, capacity=160,
-                 cuda_semantics=True):
+                 cuda_semantics=True, max_pairs=32):
         lib = library()
-        self._h = lib.avbd_oracle_create(str(model).encode(), int(num_envs), float(dt),
-                                         int(iterations), int(bool(fp64)), int(capacity))
+        self._h = lib.avbd_oracle_create_ex(str(model).encode(), int(num_envs), float(dt),
+                                            int(iterations), int(bool(fp64)), int(capacity), int(max_pairs))
         if not self._h:
             raise ValueError(lib.avbd_oracle_last_error().decode())
         info = np.zeros(6, np.int32)
