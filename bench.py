@@ -14,6 +14,10 @@ between timed steps, outside the timed events.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+
+``--workload config3`` and ``--workload config5`` time the other BASELINE
+configurations (extensions beyond the reference; see run_extended); the
+default, config 2, is the headline line.
 """
 
 from __future__ import annotations
@@ -237,6 +241,123 @@ def reference_arm(args, rank, world):
         print(json.dumps(line), flush=True)
 
 
+def run_extended(args, rank, world, local, device):
+    """BASELINE configs 3 and 5 on the synthetic biped (both beyond the
+    reference's envelope: 91 body-collision pairs; per-env parameters).
+
+    config3: 16384 envs per GPU, self-contact on (all 91 non-adjacent link
+      pairs), the BAM servo of the synthetic bundle (4 N m/rad, 0.1 N m s/rad,
+      0.5 N m cap, load-dependent friction), dt 5 ms, decimation 4,
+      10 iterations.  A step is one BamEnv.step (CUDA graph: servo, physics
+      and bookkeeping per substep, reward and observations) with actions
+      N(0, 0.1) fixed per env, auto-reset on.
+    config5: 65536 envs per GPU, 20 iterations, per-env link masses
+      x U[0.8, 1.2] (inertias alike) and ground friction U[0.4, 1.2]; each
+      step 2 % of the envs reset with joint offsets N(0, 0.02 rad) and 2 %
+      receive a base push N(0, 0.5 m/s) (a base force m dv / t held over the
+      step); PD targets swing the legs through a crouch-and-extend cycle
+      (jump-like), dt 5 ms, 4 substeps.
+    value = envs x physics substeps x K / device seconds, max over ranks."""
+    import torch
+
+    from duck_gym_b200 import CudaBatch, biped
+    from duck_gym_b200.sharding import max_over_ranks, rank_seed, weak_shard
+
+    envs_total = args.envs if args.envs != ENVS else (16384 if args.workload == "config3" else 65536)
+    envs = weak_shard(envs_total * world, rank, world).count
+    gen = torch.Generator(device=device).manual_seed(rank_seed(0, rank))
+    stream = torch.cuda.current_stream(device)
+    with tempfile.TemporaryDirectory() as d:
+        if args.workload == "config3":
+            from duck_gym_b200.bam_env import BamEnv
+
+            biped.write_bam(d, seed=0, self_contacts=True)
+            env = BamEnv(d, num_envs=envs, iterations=10, auto_reset=True, reward_enabled=True, device=local,
+                         max_pairs=128, seconds=20.0)
+            actions = 0.1 * torch.randn(envs, 14, generator=gen, device=device)
+            substeps = env.decimation
+
+            def one_step():
+                env.step(actions)
+
+            launches = lambda: env.native.launches
+            cfg = {"workload": "config 3: synthetic biped (seed 0), 91 self-contact pairs, BAM servo (4 N m/rad, "
+                               "0.1 N m s/rad, 0.5 N m), BamEnv step with auto-reset, actions N(0,0.1) fixed",
+                   "envs_per_gpu": envs, "substeps_per_step": substeps, "iterations": 10, "dt": env.dt}
+        else:
+            path = biped.write(d, seed=0)
+            meta = json.loads((Path(d) / "metadata.json").read_text())
+            text = Path(path).read_text()
+            batch = CudaBatch(str(path), envs, DT, 20, local)
+            lines = text.splitlines()
+            nb, nj, ns = (int(v) for v in lines[0].split()[2:5])
+            mass0 = torch.tensor([float(lines[2 + b].split()[1]) for b in range(nb)], device=device)
+            inertia0 = torch.tensor([[float(v) for v in lines[2 + b].split()[2:5]] for b in range(nb)], device=device)
+            scale = 0.8 + 0.4 * torch.rand(envs, nb, generator=gen, device=device)
+            friction = (0.4 + 0.8 * torch.rand(envs, 1, generator=gen, device=device)).expand(envs, ns).contiguous()
+            mass = (mass0 * scale).contiguous()
+            batch.set_parameters(mass, (inertia0 * scale[..., None]).contiguous(), friction)
+            home = torch.tensor(meta["home"], device=device)
+            legs = torch.zeros(14, device=device)
+            for name, a in (("hip_pitch", -0.4), ("knee", 0.8), ("ankle", -0.4)):
+                for j, n in enumerate(meta["joint_names"]):
+                    if name in n:
+                        legs[j] = a
+            phase = 2 * math.pi * torch.rand(envs, 1, generator=gen, device=device)
+            kp, limit = meta["kp"], meta["torque_limit"]
+            forces = torch.zeros(envs, 3, device=device)
+            substeps = SUBSTEPS
+            counter = [0]
+
+            def one_step():
+                k = counter[0]
+                counter[0] += 1
+                cycle = 0.5 - 0.5 * torch.cos(phase + 2 * math.pi * k * SUBSTEPS * DT / 0.6)
+                target = (home + legs * cycle).contiguous()
+                reset = torch.rand(envs, generator=gen, device=device) < 0.02
+                q = (home + 0.02 * torch.randn(envs, 14, generator=gen, device=device)).contiguous()
+                batch.reset(reset, q, torch.zeros(envs, 6, device=device))
+                push = torch.rand(envs, 1, generator=gen, device=device) < 0.02
+                dv = 0.5 * torch.randn(envs, 3, generator=gen, device=device)
+                torch.where(push, dv * mass[:, 1:2] / (SUBSTEPS * DT), torch.zeros_like(dv), out=forces)
+                batch.step(target, forces, SUBSTEPS, kp, limit)
+
+            launches = lambda: batch.launches
+            cfg = {"workload": "config 5: synthetic biped (seed 0), per-env masses x U[0.8,1.2] and ground friction "
+                               "U[0.4,1.2], 2% resets/step with joint offsets N(0,0.02), 2% base pushes N(0,0.5 m/s), "
+                               "crouch-and-extend PD targets",
+                   "envs_per_gpu": envs, "substeps_per_step": SUBSTEPS, "iterations": 20, "dt": DT}
+        for _ in range(SETTLE // 4 + args.warmup):
+            one_step()
+        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        clocks = ClockSampler(local)
+        clocks.start()
+        l0 = launches()
+        torch.cuda.synchronize(device)
+        t_start = time.monotonic()
+        for k in range(args.steps):
+            flush.zero_()
+            starts[k].record(stream)
+            one_step()
+            ends[k].record(stream)
+        torch.cuda.synchronize(device)
+        clocks.window = (t_start, time.monotonic())
+        clocks.stop()
+        device_s = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3
+        slowest = max_over_ranks(device_s, device)
+        value = envs * substeps * args.steps * world / slowest
+        if rank == 0:
+            cfg.update({"l2": "flushed between timed steps (256 MiB write, outside the timed events)",
+                        "parallelism": f"env shards x{world}, no physics communication"})
+            print(json.dumps({
+                "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1e3 * slowest / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded biped, no dataset)",
+                "config": cfg, "gpu_launches": launches() - l0, "clocks": clocks.summary()}), flush=True)
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -245,6 +366,7 @@ def main():
     p.add_argument("--envs", type=int, default=ENVS)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=["config2", "config3", "config5"], default="config2")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -267,6 +389,13 @@ def main():
 
     from duck_gym_b200 import CudaBatch, fp32_peak_tflops
     from duck_gym_b200.sharding import max_over_ranks, rank_seed, weak_shard
+
+    if args.workload != "config2":
+        run_extended(args, rank, world, local, device)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     with tempfile.TemporaryDirectory() as d:
         model, meta = make_model(d)

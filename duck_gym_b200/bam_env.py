@@ -110,7 +110,7 @@ class _RewardState:
 class BamEnv:
     def __init__(self, model_dir, num_envs=1, backend="cuda", fp64=False, iterations=200, auto_reset=False,
                  seconds=40.0, seed=42, reward_enabled=False, source_iteration=0, training=None, heading_hold=False,
-                 physics_dt=None, device=0, use_graph=True):
+                 physics_dt=None, device=0, use_graph=True, max_pairs=32):
         # Validation and settings follow bam_env.py:17-133.
         if backend != "cuda":
             raise ValueError("duck_gym_b200 runs on CUDA only; the CPU path is the reference's own solver")
@@ -162,7 +162,7 @@ class BamEnv:
         center = limits.mean(-1, keepdim=True)
         self.soft_limits = (center + 0.9 * (limits - center))[None, :, :].expand(E, -1, -1)
         self._model_dir = Path(model_dir)
-        self.native = CudaBatch(model, E, self.dt, iterations, device, fp64)
+        self.native = CudaBatch(model, E, self.dt, iterations, device, fp64, max_pairs=max_pairs)
         J = self.native.num_joints
         if J != 14 or len(self.foot_ids) != 2:
             raise ValueError("The BAM environment needs the 14-joint biped with two feet")
