@@ -241,6 +241,88 @@ def reference_arm(args, rank, world):
         print(json.dumps(line), flush=True)
 
 
+COMMAND_RANGES = [[-0.3, 0.3], [-0.3, 0.3], [-1.0, 1.0]]
+
+
+def run_ppo(args, rank, world, local, device):
+    """full RL rollout plus PPO update.  4096 BamEnv envs
+    per GPU (the synthetic bundle, dt 5 ms, decimation 4, 10 iterations) on a
+    velocity-command task, commands U[-0.3,0.3] m/s in x/y and U[-1,1] rad/s
+    in yaw; actor MLP 61-512-256-128-14 ELU under bf16 autocast (the actor
+    observation has 51 live entries -- angular velocity, gravity, joint
+    positions and velocities, last action, command -- plus the reference's 10
+    zero pads; BASELINE's "48-dim" does not add up to its own list); 24-step
+    rollouts, 5 epochs x 4 minibatches; gradients averaged over the ranks by
+    bucketed NCCL all-reduces overlapped with backward.  One step = one PPO
+    iteration; value = envs x 24 x 4 physics steps per iteration x ranks /
+    slowest rank's device seconds."""
+    import torch
+    import torch.distributed as dist
+
+    from duck_gym_b200 import biped
+    from duck_gym_b200.bam_env import BamEnv
+    from duck_gym_b200.ppo import PPO, PPOConfig
+    from duck_gym_b200.sharding import max_over_ranks, rank_seed
+
+    envs = args.envs
+    training = dict(command_ranges=COMMAND_RANGES, command_resample_seconds=5.0, reset_joint_noise=0.01,
+                    reset_tilt_noise=0.01, horizontal_velocity_variance=0.1, vertical_velocity_variance=0.1)
+    stream = torch.cuda.current_stream(device)
+    with tempfile.TemporaryDirectory() as d:
+        biped.write_bam(d, seed=0)
+        env = BamEnv(d, num_envs=envs, iterations=10, auto_reset=True, reward_enabled=True, device=local,
+                     training=training, seed=rank_seed(0, rank), seconds=20.0)
+        agent = PPO(env, PPOConfig(), device=device, seed=rank_seed(1, rank))
+        for _ in range(args.warmup):
+            agent.rollout()
+            agent.update()
+        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        rollout_ms, update_ms = [], []
+        clocks = ClockSampler(local)
+        clocks.start()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        t_start = time.monotonic()
+        for k in range(args.steps):
+            flush.zero_()
+            mid = torch.cuda.Event(enable_timing=True)
+            starts[k].record(stream)
+            agent.rollout()
+            mid.record(stream)
+            stats = agent.update()
+            ends[k].record(stream)
+            torch.cuda.synchronize(device)
+            rollout_ms.append(starts[k].elapsed_time(mid))
+            update_ms.append(mid.elapsed_time(ends[k]))
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        clocks.window = (t_start, time.monotonic())
+        clocks.stop()
+        device_s = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / 1e3
+        slowest = max_over_ranks(device_s, device)
+        physics = envs * agent.cfg.steps_per_env * env.decimation
+        value = physics * args.steps * world / slowest
+        if rank == 0:
+            print(json.dumps({
+                "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1e3 * slowest / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32 physics, bf16 actor/critic",
+                "data": "synthetic (seeded biped, no dataset)",
+                "config": {"workload": "config 4: PPO rollout (24 steps) + update (5 epochs x 4 minibatches) on the "
+                                       "BAM velocity-command task, actor 61-512-256-128-14 ELU bf16",
+                           "envs_per_gpu": envs, "substeps_per_step": env.decimation, "iterations": 10, "dt": env.dt,
+                           "rollout_ms": statistics.mean(rollout_ms), "update_ms": statistics.mean(update_ms),
+                           "samples_per_iteration": envs * agent.cfg.steps_per_env * world,
+                           "last_update": stats,
+                           "l2": "flushed between timed iterations (256 MiB write, outside the timed events)",
+                           "parallelism": f"dp{world}: env shards, NCCL gradient all-reduce"},
+                "clocks": clocks.summary()}), flush=True)
+
+
 def run_extended(args, rank, world, local, device):
     """BASELINE configs 3 and 5 on the synthetic biped (both beyond the
     reference's envelope: 91 body-collision pairs; per-env parameters).
@@ -263,6 +345,8 @@ def run_extended(args, rank, world, local, device):
     from duck_gym_b200 import CudaBatch, biped
     from duck_gym_b200.sharding import max_over_ranks, rank_seed, weak_shard
 
+    if args.workload == "config4":
+        return run_ppo(args, rank, world, local, device)
     envs_total = args.envs if args.envs != ENVS else (16384 if args.workload == "config3" else 65536)
     envs = weak_shard(envs_total * world, rank, world).count
     gen = torch.Generator(device=device).manual_seed(rank_seed(0, rank))
@@ -366,7 +450,7 @@ def main():
     p.add_argument("--envs", type=int, default=ENVS)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=["config2", "config3", "config5"], default="config2")
+    p.add_argument("--workload", choices=["config2", "config3", "config4", "config5"], default="config2")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -349,10 +349,19 @@ class BamEnv:
             self._call("duck_bam_observe", None, 1)
 
     def resample_commands(self, mask):
-        """bam_env.py:213-218 (one draw for every env, masked assignment)."""
-        commands = self.home.new_tensor(self.training["commands"])
-        indices = torch.randint(len(commands), (self.num_envs,), generator=self.generator, device=self.device)
-        self.command.copy_(torch.where(mask[:, None], commands[indices], self.command))
+        """bam_env.py:213-218 (one draw for every env, masked assignment).
+        Extension: a training dictionary with ``command_ranges`` [[lo, hi]] x 3
+        draws (vx, vy, yaw rate) uniformly instead of from a command list."""
+        ranges = self.training.get("command_ranges")
+        if ranges is not None:
+            r = self.home.new_tensor(ranges)
+            u = torch.rand((self.num_envs, 3), generator=self.generator, device=self.device, dtype=self.dtype)
+            fresh = r[:, 0] + (r[:, 1] - r[:, 0]) * u
+        else:
+            commands = self.home.new_tensor(self.training["commands"])
+            indices = torch.randint(len(commands), (self.num_envs,), generator=self.generator, device=self.device)
+            fresh = commands[indices]
+        self.command.copy_(torch.where(mask[:, None], fresh, self.command))
 
     def failure_mask(self):
         """bam_env.py:409-418, as evaluated at the end of the last step."""

@@ -1,0 +1,289 @@
+"""PPO rollout and update for the native environments.
+
+The reference trains with rsl-rl 5's ``OnPolicyRunner`` and ``PPO``
+(scripts/train_bam_native.py:14-140) configured from mjlab's
+``Mjlab-Velocity-Flat-MicroDuck`` task; neither package is available here.
+This module restates rsl-rl's published PPO algorithm in plain torch:
+
+* a Gaussian policy with a scalar (state-independent) std, as the reference
+  pins (train_bam_native.py:127-129), actor and critic MLPs with ELU;
+* rollouts of ``steps_per_env`` steps; time-out bootstrapping of the reward
+  (r += gamma V(s) on time-outs); GAE(gamma, lambda) returns;
+* ``epochs`` x ``mini_batches`` updates of the clipped surrogate, the clipped
+  value loss and an entropy bonus, with the adaptive KL learning-rate
+  schedule and gradient-norm clipping;
+* the actor runs under bf16 autocast (tensor cores) in the rollout and the
+  update, with fp32 master weights;
+* with a process group of several ranks, gradients are averaged across
+  ranks by NCCL all-reduces of flat buckets, launched from gradient hooks as
+  soon as a bucket is complete (overlapping the rest of the backward pass),
+  and the KL used by the schedule is averaged too, so every rank takes the
+  same step.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+
+@dataclass
+class PPOConfig:
+    steps_per_env: int = 24
+    epochs: int = 5
+    mini_batches: int = 4
+    gamma: float = 0.99
+    lam: float = 0.95
+    clip: float = 0.2
+    value_coef: float = 1.0
+    entropy_coef: float = 0.005
+    learning_rate: float = 3e-4
+    desired_kl: float = 0.01
+    max_grad_norm: float = 1.0
+    initial_std: float = 0.15
+    actor_hidden: tuple = (512, 256, 128)
+    critic_hidden: tuple = (512, 256, 128)
+    bf16: bool = True
+    bucket_mb: float = 0.5
+
+
+def mlp(sizes):
+    layers = []
+    for i in range(len(sizes) - 1):
+        layers.append(nn.Linear(sizes[i], sizes[i + 1]))
+        if i < len(sizes) - 2:
+            layers.append(nn.ELU())
+    return nn.Sequential(*layers)
+
+
+class ActorCritic(nn.Module):
+    def __init__(self, actor_obs, critic_obs, actions, cfg: PPOConfig):
+        super().__init__()
+        self.actor = mlp([actor_obs, *cfg.actor_hidden, actions])
+        self.critic = mlp([critic_obs, *cfg.critic_hidden, 1])
+        self.std = nn.Parameter(torch.full((actions,), float(cfg.initial_std)))
+        self.bf16 = cfg.bf16
+
+    def _autocast(self, x):
+        return torch.autocast(x.device.type, dtype=torch.bfloat16, enabled=self.bf16)
+
+    def mean(self, obs):
+        with self._autocast(obs):
+            return self.actor(obs).float()
+
+    def value(self, obs):
+        with self._autocast(obs):
+            return self.critic(obs).float().squeeze(-1)
+
+    def distribution(self, obs):
+        return torch.distributions.Normal(self.mean(obs), self.std.expand(obs.shape[0], -1))
+
+
+class Storage:
+    """Rollout buffers [T, E, ...] (rsl-rl RolloutStorage)."""
+
+    def __init__(self, T, E, actor_obs, critic_obs, actions, device):
+        z = lambda *s: torch.zeros(*s, device=device)
+        self.obs, self.critic_obs = z(T, E, actor_obs), z(T, E, critic_obs)
+        self.actions, self.log_prob, self.mu = z(T, E, actions), z(T, E), z(T, E, actions)
+        self.sigma = z(T, E, actions)
+        self.rewards, self.dones, self.values = z(T, E), z(T, E), z(T, E)
+        self.returns, self.advantages = z(T, E), z(T, E)
+        self.T, self.E, self.step = T, E, 0
+
+
+def gae(rewards, dones, values, last_values, gamma, lam):
+    """GAE returns and advantages (rsl-rl RolloutStorage.compute_returns):
+    delta_t = r_t + gamma (1 - d_t) V_{t+1} - V_t,
+    A_t = delta_t + gamma lambda (1 - d_t) A_{t+1},  R_t = A_t + V_t."""
+    T = rewards.shape[0]
+    returns = torch.empty_like(rewards)
+    advantage = torch.zeros_like(last_values)
+    for t in reversed(range(T)):
+        next_values = last_values if t == T - 1 else values[t + 1]
+        live = 1.0 - dones[t]
+        delta = rewards[t] + live * gamma * next_values - values[t]
+        advantage = delta + live * gamma * lam * advantage
+        returns[t] = advantage + values[t]
+    return returns, returns - values
+
+
+def ppo_loss(policy, obs, critic_obs, actions, old_log_prob, old_mu, old_sigma, target_values, returns, advantages,
+             cfg: PPOConfig):
+    """Clipped surrogate + clipped value loss - entropy bonus (rsl-rl
+    PPO.update); also the mean KL of the new policy to the old one."""
+    dist_new = policy.distribution(obs)
+    log_prob = dist_new.log_prob(actions).sum(-1)
+    entropy = dist_new.entropy().sum(-1)
+    mu, sigma = dist_new.mean, dist_new.stddev
+    value = policy.value(critic_obs)
+    kl = (torch.log(sigma / old_sigma + 1e-5)
+          + (old_sigma.square() + (old_mu - mu).square()) / (2.0 * sigma.square()) - 0.5).sum(-1).mean()
+    ratio = torch.exp(log_prob - old_log_prob)
+    surrogate = torch.max(-advantages * ratio, -advantages * ratio.clamp(1.0 - cfg.clip, 1.0 + cfg.clip)).mean()
+    clipped = target_values + (value - target_values).clamp(-cfg.clip, cfg.clip)
+    value_loss = torch.max((value - returns).square(), (clipped - returns).square()).mean()
+    loss = surrogate + cfg.value_coef * value_loss - cfg.entropy_coef * entropy.mean()
+    return loss, dict(surrogate=surrogate.detach(), value=value_loss.detach(), entropy=entropy.mean().detach(),
+                      kl=kl.detach())
+
+
+class GradientAllReduce:
+    """Averages gradients over the ranks of the default process group with one
+    in-place all-reduce per bucket of about ``bucket_mb`` MB, issued from
+    gradient hooks as soon as every parameter of the bucket has its gradient,
+    so communication overlaps the rest of the backward pass."""
+
+    def __init__(self, params, bucket_mb):
+        self.world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+        self.params = [p for p in params if p.requires_grad]
+        self.buckets, self.handles, self.pending = [], [], {}
+        if self.world == 1:
+            return
+        limit = max(1, int(bucket_mb * 1e6 / 4))
+        bucket, size = [], 0
+        for p in reversed(self.params):     # gradients arrive roughly in reverse order
+            bucket.append(p)
+            size += p.numel()
+            if size >= limit:
+                self.buckets.append(bucket)
+                bucket, size = [], 0
+        if bucket:
+            self.buckets.append(bucket)
+        self.flat = [torch.zeros(sum(p.numel() for p in b), device=b[0].device) for b in self.buckets]
+        self.owner = {}
+        for i, b in enumerate(self.buckets):
+            for p in b:
+                self.owner[p] = i
+                p.register_post_accumulate_grad_hook(self._ready)
+
+    def _ready(self, p):
+        i = self.owner[p]
+        self.pending[i] = self.pending.get(i, 0) + 1
+        if self.pending[i] == len(self.buckets[i]):
+            flat, offset = self.flat[i], 0
+            for q in self.buckets[i]:
+                n = q.numel()
+                flat[offset:offset + n].copy_(q.grad.reshape(-1))
+                offset += n
+            self.handles.append((i, dist.all_reduce(flat, async_op=True)))
+
+    def finish(self):
+        """Wait for the bucket all-reduces and write the averages back."""
+        if self.world == 1:
+            return
+        if len(self.handles) != len(self.buckets):
+            raise RuntimeError("a gradient bucket was not reduced (unused parameters?)")
+        for i, handle in self.handles:
+            handle.wait()
+            flat, offset = self.flat[i], 0
+            flat.div_(self.world)
+            for q in self.buckets[i]:
+                n = q.numel()
+                q.grad.copy_(flat[offset:offset + n].view_as(q.grad))
+                offset += n
+        self.handles, self.pending = [], {}
+
+
+class PPO:
+    """Rollout and update over an env with the rsl-rl VecEnv contract:
+    ``get_observations()`` -> {"actor", "critic"} (or a tensor), ``step(actions)``
+    -> (obs, reward, done, info) with ``info["time_outs"]``."""
+
+    def __init__(self, env, cfg: PPOConfig | None = None, device=None, seed=0):
+        self.cfg = cfg or PPOConfig()
+        self.env = env
+        self.device = torch.device(device or getattr(env, "device", "cuda"))
+        torch.manual_seed(seed)
+        obs = self._split(env.get_observations())
+        self.obs, self.critic_obs = obs
+        self.policy = ActorCritic(self.obs.shape[1], self.critic_obs.shape[1], env.num_actions, self.cfg).to(
+            self.device)
+        self.world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+        if self.world > 1:
+            for p in self.policy.parameters():   # every rank starts from rank 0's weights
+                dist.broadcast(p.data, 0)
+        self.reducer = GradientAllReduce(self.policy.parameters(), self.cfg.bucket_mb)
+        self.optimizer = torch.optim.Adam(self.policy.parameters(), lr=self.cfg.learning_rate)
+        self.learning_rate = self.cfg.learning_rate
+        self.storage = Storage(self.cfg.steps_per_env, env.num_envs, self.obs.shape[1], self.critic_obs.shape[1],
+                               env.num_actions, self.device)
+
+    def _split(self, out):
+        obs = out[0] if isinstance(out, tuple) else out
+        if isinstance(obs, dict):
+            return obs["actor"].to(self.device), obs["critic"].to(self.device)
+        return obs.to(self.device), obs.to(self.device)
+
+    @torch.no_grad()
+    def rollout(self):
+        s, cfg = self.storage, self.cfg
+        for t in range(cfg.steps_per_env):
+            d = self.policy.distribution(self.obs)
+            actions = d.sample()
+            s.obs[t], s.critic_obs[t] = self.obs, self.critic_obs
+            s.actions[t] = actions
+            s.log_prob[t] = d.log_prob(actions).sum(-1)
+            s.mu[t], s.sigma[t] = d.mean, d.stddev
+            s.values[t] = self.policy.value(self.critic_obs)
+            obs, reward, done, info = self.env.step(actions)
+            reward = reward.to(self.device).float()
+            if "time_outs" in info:
+                reward = reward + cfg.gamma * s.values[t] * info["time_outs"].to(self.device).float()
+            s.rewards[t] = reward
+            s.dones[t] = done.to(self.device).float()
+            self.obs, self.critic_obs = self._split(obs)
+        last = self.policy.value(self.critic_obs)
+        s.returns, s.advantages = gae(s.rewards, s.dones, s.values, last, cfg.gamma, cfg.lam)
+        a = s.advantages
+        s.advantages = (a - a.mean()) / (a.std() + 1e-8)
+
+    def update(self, generator=None):
+        s, cfg = self.storage, self.cfg
+        n = s.T * s.E
+        flat = lambda x: x.reshape(n, *x.shape[2:])
+        data = [flat(x) for x in (s.obs, s.critic_obs, s.actions, s.log_prob, s.mu, s.sigma, s.values, s.returns,
+                                  s.advantages)]
+        size = n // cfg.mini_batches
+        stats = []
+        for _ in range(cfg.epochs):
+            order = torch.randperm(n, device=self.device, generator=generator)
+            for b in range(cfg.mini_batches):
+                idx = order[b * size:(b + 1) * size]
+                loss, info = ppo_loss(self.policy, *[x[idx] for x in data], cfg)
+                self._adapt(info["kl"])
+                self.optimizer.zero_grad(set_to_none=False)
+                loss.backward()
+                self.reducer.finish()
+                nn.utils.clip_grad_norm_(self.policy.parameters(), cfg.max_grad_norm)
+                self.optimizer.step()
+                stats.append(info)
+        return {k: torch.stack([x[k] for x in stats]).mean().item() for k in stats[0]}
+
+    def _adapt(self, kl):
+        """rsl-rl's adaptive schedule: lr / 1.5 above 2 x desired KL, x 1.5
+        below half of it (the KL averaged over ranks)."""
+        if self.cfg.desired_kl is None:
+            return
+        if self.world > 1:
+            kl = kl.clone()
+            dist.all_reduce(kl)
+            kl /= self.world
+        kl = float(kl)
+        if kl > 2.0 * self.cfg.desired_kl:
+            self.learning_rate = max(1e-5, self.learning_rate / 1.5)
+        elif 0.0 < kl < self.cfg.desired_kl / 2.0:
+            self.learning_rate = min(1e-2, self.learning_rate * 1.5)
+        for group in self.optimizer.param_groups:
+            group["lr"] = self.learning_rate
+
+    def learn(self, iterations):
+        history = []
+        for _ in range(iterations):
+            self.rollout()
+            history.append(self.update())
+        return history
