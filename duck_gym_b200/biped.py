@@ -354,6 +354,41 @@ def write_bam(directory, seed: int = 0, self_contacts: bool = False, **kwargs):
     return directory
 
 
+def gait_record(text: str, meta: dict, samples: int = 32, period: float = 0.8, lift: float = 0.008,
+                speed: float = 0.05) -> dict:
+    """A synthetic ``gait.npz`` record with the keys the reference's tensor
+    env reads (python/duck_gym/tensor_env.py:152-171; written from MuJoCo
+    inverse kinematics by scripts/prepare_gait.py:120-131 there):
+    ``targets`` [4 directions (+x, -x, +y, -y), samples, J] -- HOME plus a
+    stepping cycle (hip pitch / roll swing and knee lift, legs half a period
+    apart) -- ``foot_collision_points`` [2, 8, 3] (the foot boxes' corners in
+    body coordinates), ``foot_bodies`` [2], ``period``, ``lift``, ``speed``."""
+    home = np.asarray(meta["home"], dtype=float)
+    names = list(meta["joint_names"])
+    phase = 2 * np.pi * np.arange(samples) / samples
+    table = np.repeat(home[None, None, :], 4, axis=0).repeat(samples, axis=1)
+    for d, (axis, sign) in enumerate(((0, 1), (0, -1), (1, 1), (1, -1))):
+        for side, shift in (("left_", 0.0), ("right_", np.pi)):
+            swing = np.sin(phase + shift)
+            knee = np.clip(np.sin(phase + shift), 0, None)
+            j = names.index(side + ("hip_pitch" if axis == 0 else "hip_roll"))
+            table[d, :, j] += -sign * 0.15 * swing if axis == 0 else sign * 0.08 * swing
+            table[d, :, names.index(side + "knee")] += 0.3 * knee
+            table[d, :, names.index(side + "ankle")] -= 0.15 * knee
+    cfg = bam_config(text, meta)
+    feet = cfg["feet"]
+    return dict(targets=table, foot_collision_points=np.array([f["points"] for f in feet]),
+                foot_bodies=np.array([f["body"] for f in feet]), period=period, lift=lift, speed=speed)
+
+
+def write_gait(directory, seed: int = 0, **kwargs):
+    """Write ``gait.npz`` next to the seeded biped's model and metadata."""
+    directory = Path(directory)
+    text, meta = generate(seed)
+    np.savez_compressed(directory / "gait.npz", **gait_record(text, meta, **kwargs))
+    return directory / "gait.npz"
+
+
 def with_parameters(text: str, mass=None, inertia=None, friction=None) -> str:
     """The model text with one environment's physical parameters substituted:
     body masses [B], principal inertias [B,3] and shape frictions [S] (None

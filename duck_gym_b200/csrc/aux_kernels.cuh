@@ -194,6 +194,25 @@ __device__ __forceinline__ V3<R> envGroundForce(const DevModel<R> *m, const R *r
   return f;
 }
 
+// Total contact force on one body (ground and body-pair contacts, the pair's
+// reaction with the opposite sign), summed in contact order as
+// contactForcesKernel does with ground_only off.
+template <class R>
+__device__ __forceinline__ V3<R> envBodyForce(const DevModel<R> *m, const R *rec, int body) {
+  const R *cs = recContacts(m, rec);
+  const int n = int(rec[1]);
+  V3<R> f{R(0), R(0), R(0)};
+  for (int i = 0; i < n; ++i) {
+    const R *c = cs + kRecContact * i;
+    const int a = int(c[0]), o = int(c[3]);
+    if (a != body && o != body) continue;
+    V3<R> g = -recContactWorld(c, V3<R>{c[26], c[27], c[28]});
+    if (a == body) { f.x += g.x; f.y += g.y; f.z += g.z; }
+    if (o == body) { f.x -= g.x; f.y -= g.y; f.z -= g.z; }
+  }
+  return f;
+}
+
 // BasicState::generalizedLoads (kernel.cuh:504-554): RNEA at zero joint
 // acceleration for one environment; out [J,3] = (bias, contact + limit,
 // applied actuator) per hinge.

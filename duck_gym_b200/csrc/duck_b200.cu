@@ -590,6 +590,24 @@ EnvKernelParams envParams(const duck_batch *b, const duck_env_params *p) {
   k.sigma2 = p->tracking_sigma * p->tracking_sigma;
   k.phaseRate = 2 * 3.14159265358979323846 / p->gait_period;
   for (int i = 0; i < 4; ++i) k.iquat[i] = p->iquat[i];
+  k.gait = p->gait;
+  k.footClearance = p->foot_clearance;
+  k.loadTransfer = p->load_transfer;
+  if (p->gait) require(p->gait_table != nullptr && p->gait_samples > 0, "Gait shaping needs the gait table");
+  if (p->foot_clearance) require(p->foot_xyz != nullptr && p->foot_points > 0, "Foot clearance needs foot points");
+  if (p->foot_clearance || p->load_transfer)
+    require(p->foot_body[0] > 0 && p->foot_body[0] < b->nb && p->foot_body[1] > 0 && p->foot_body[1] < b->nb &&
+                (!p->load_transfer || p->mass > 0),
+            "Invalid foot bodies or mass");
+  k.gaitSamples = p->gait_samples;
+  k.footPoints = p->foot_points;
+  k.footBody[0] = p->foot_body[0];
+  k.footBody[1] = p->foot_body[1];
+  k.gaitPeriod = p->gait_period;
+  k.gaitLift = p->gait_lift;
+  k.massG = p->mass * 9.81;
+  k.gaitTable = p->gait_table;
+  k.footXyz = p->foot_xyz;
   return k;
 }
 }  // namespace
@@ -619,6 +637,31 @@ int duck_env_targets(duck_batch *b, const void *actions, double scale, const voi
           static_cast<const float *>(upper), static_cast<float *>(a_out), static_cast<float *>(target_out));
     ++b->launches;
     check(cudaGetLastError(), "env targets");
+  });
+}
+
+int duck_env_reference_targets(duck_batch *b, const duck_env_params *params, const void *actions, double scale,
+                               const void *home, const void *lower, const void *upper, const int64_t *episode_length,
+                               const void *commands, void *a_out, void *target_out, duck_stream stream) {
+  return guarded([&] {
+    require(b && actions && home && lower && upper && episode_length && commands && a_out && target_out,
+            "Invalid arguments");
+    const EnvKernelParams k = envParams(b, params);
+    DeviceGuard guard(b->device);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int items = b->n * b->nj;
+    if (items == 0) return;
+    auto run = [&](auto zero) {
+      using R = decltype(zero);
+      envGaitTargetsKernel<R><<<blocksFor(items, 256), 256, 0, s>>>(
+          b->n, k, static_cast<const R *>(actions), R(scale), static_cast<const R *>(home),
+          static_cast<const R *>(lower), static_cast<const R *>(upper),
+          reinterpret_cast<const long long *>(episode_length), static_cast<const R *>(commands),
+          static_cast<R *>(a_out), static_cast<R *>(target_out));
+    };
+    if (b->fp64) run(0.0); else run(0.0f);
+    ++b->launches;
+    check(cudaGetLastError(), "env reference targets");
   });
 }
 

@@ -25,6 +25,12 @@ struct EnvKernelParams {
   double rootHeight, controlDt, velocityAlpha, trackingWeight, headingWeight, sigma2, phaseRate;
   float tilt;  // -cos(0.5) as a float32 tensor
   double iquat[4];
+  // Gait shaping (tensor_env.py:152-171, 263-277, 318-344).
+  int gait, footClearance, loadTransfer, gaitSamples, footPoints;
+  int footBody[2];
+  double gaitPeriod, gaitLift, massG;
+  const void *gaitTable;    // [4, samples, J] Real
+  const void *footXyz;      // [2, P, 3] Real
 };
 
 // Torch CPU cross product: fma(a_i, b_j, -(a_j b_i)).
@@ -106,7 +112,7 @@ __device__ __forceinline__ void envWriteObs(const DevModel<R> *m, const R *rec, 
     obs[o++] = float(commands[1]);
     obs[o++] = float(f.yaw0);
     obs[o++] = float(f.yaw1);
-    R phase = R(len) * R(p.controlDt) * R(p.phaseRate);
+    R phase = R(len) * R(p.controlDt) * R(p.phaseRate);   // phaseRate = 2 pi / gait period
     obs[o++] = float(sin(phase));
     obs[o++] = float(cos(phase));
   }
@@ -126,6 +132,84 @@ __global__ void envTargetsKernel(int count, int nj, const R *actions, R scale, c
   R a = rclamp(actions[i], R(-1), R(1));
   aOut[i] = a;
   targetOut[i] = rmin(rmax(xadd(home[j], xmul(scale, a)), lower[j]), upper[j]);
+}
+
+// tensor_env.py:263-283 with the gait table: reference target of each env
+// (the table at the episode phase, in the direction the command points to,
+// blended in over the first second), then the clamped PD target.  One thread
+// per (env, joint).
+template <class R>
+__global__ void envGaitTargetsKernel(int count, EnvKernelParams p, const R *actions, R scale, const R *home,
+                                     const R *lower, const R *upper, const long long *episodeLength,
+                                     const R *commands, R *aOut, R *targetOut) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int nj = p.nj;
+  if (i >= count * nj) return;
+  const int e = i / nj, j = i % nj;
+  const R len = R(episodeLength[e]);
+  R ref = home[j];
+  if (p.gait) {
+    const R phase = len * R(p.controlDt) / R(p.gaitPeriod);
+    const int n = p.gaitSamples;
+    const R index = (phase - floor(phase)) * R(n);
+    const int lo = int(index);
+    const R fraction = index - R(lo);
+    const R cx = commands[2 * size_t(e)], cy = commands[2 * size_t(e) + 1];
+    // argmax over the directions (+x, -x, +y, -y), first one on ties.
+    const R dots[4] = {cx, -cx, cy, -cy};
+    int d = 0;
+    for (int k = 1; k < 4; ++k)
+      if (dots[k] > dots[d]) d = k;
+    const R *table = static_cast<const R *>(p.gaitTable) + size_t(d) * n * nj;
+    const R r = table[size_t(lo) * nj + j] * (R(1) - fraction) + table[size_t((lo + 1) % n) * nj + j] * fraction;
+    const R blend = rmin(rmax(len * R(p.controlDt), R(0)), R(1));
+    ref = home[j] + (r - home[j]) * blend;
+  }
+  const R a = rclamp(actions[i], R(-1), R(1));
+  aOut[i] = a;
+  targetOut[i] = rmin(rmax(xadd(ref, xmul(scale, a)), lower[j]), upper[j]);
+}
+
+// Foot-clearance and load-transfer shaping (tensor_env.py:318-344), added to
+// the reward before the failure override.
+template <class R>
+__device__ __forceinline__ R gaitShaping(const DevModel<R> *m, const R *rec, const EnvKernelParams &p, long long len) {
+  const R *bodies = rec + kRecHeader;
+  R penalty = R(0);
+  if (p.footClearance) {
+    const R *pts = static_cast<const R *>(p.footXyz);
+    R sum = R(0);
+    for (int f = 0; f < 2; ++f) {
+      const R *fb = bodies + kRecBody * p.footBody[f];
+      const V3<R> up = tinverseRotate(Q4<R>{fb[3], fb[4], fb[5], fb[6]}, V3<R>{R(0), R(0), R(1)});
+      R lowest = R(INFINITY);
+      for (int v = 0; v < p.footPoints; ++v) {
+        const R *q = pts + (size_t(f) * p.footPoints + v) * 3;
+        lowest = rmin(lowest, q[0] * up.x + q[1] * up.y + q[2] * up.z + fb[2]);
+      }
+      R phase = (R(len) + R(1)) * R(p.controlDt) / R(p.gaitPeriod) + (f ? R(0.5) : R(0));
+      phase = phase - floor(phase);
+      const R swing = rmin(rmax((phase - R(0.6)) / R(0.4), R(0)), R(1));
+      const R s = sin(R(3.14159265358979323846) * swing);
+      const R desired = R(p.gaitLift) * (s * s);
+      const R err = rmax(lowest, R(0)) - desired;
+      sum += err * err;
+    }
+    penalty += R(20000) * sum;
+  }
+  if (p.loadTransfer) {
+    const R cycle = (R(len) + R(1)) * R(p.controlDt) / R(p.gaitPeriod);
+    const R left = R(0.5) + R(0.5) * sin(R(2 * 3.14159265358979323846) * (cycle - R(0.05)));
+    const R wanted[2] = {left, R(1) - left};
+    R sum = R(0);
+    for (int f = 0; f < 2; ++f) {
+      const R fz = envBodyForce(m, rec, p.footBody[f]).z / R(p.massG);
+      const R err = rmin(rmax(fz, R(0)), R(3)) - wanted[f];
+      sum += err * err;
+    }
+    penalty += R(3) * sum;
+  }
+  return penalty;
 }
 
 template <class R>
@@ -189,6 +273,7 @@ __global__ void envPostStepKernel(const DevModel<R> *__restrict__ m, const R *re
     r = R(1.5) * exp(R(-20) * g2) + exp(R(-2000) * h2) + R(0.5) * exp(R(-10) * dot(f.v, f.v)) - R(0.02) * ww -
         R(0.05) * sj - R(0.01) * sa - R(0.02) * sd;
   }
+  if (p.footClearance || p.loadTransfer) r -= gaitShaping(m, rec, p, episodeLength[e]);
   r = (failed ? R(-2) : r) * R(p.controlDt);
   const long long len = episodeLength[e] + 1;
   episodeLength[e] = len;

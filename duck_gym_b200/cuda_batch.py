@@ -74,6 +74,7 @@ def library():
         lib.duck_fp32_peak.argtypes = [I, I, ctypes.POINTER(D), P]
         lib.duck_env_obs_dim.argtypes = [P, P]
         lib.duck_env_targets.argtypes = [P, P, D, P, P, P, P, P, P]
+        lib.duck_env_reference_targets.argtypes = [P, P, P, D, P, P, P, P, P, P, P, P]
         lib.duck_env_post_step.argtypes = [P] * 17
         lib.duck_env_observe.argtypes = [P] * 9
         lib.duck_env_reset_buffers.argtypes = [P] * 10
@@ -90,7 +91,7 @@ def library():
                      "duck_batch_self_contact_stats", "duck_batch_contact_counts",
                      "duck_batch_generalized_loads", "duck_batch_reference", "duck_batch_export",
                      "duck_batch_import", "duck_batch_contact_keys", "duck_fp32_peak", "duck_env_obs_dim",
-                     "duck_env_targets", "duck_env_post_step", "duck_env_observe", "duck_env_reset_buffers",
+                     "duck_env_targets", "duck_env_reference_targets", "duck_env_post_step", "duck_env_observe", "duck_env_reset_buffers",
                      "duck_bam_critic_dim", "duck_bam_step", "duck_bam_begin", "duck_bam_substep", "duck_bam_finish",
                      "duck_bam_servo", "duck_bam_reset_buffers", "duck_bam_observe"):
             getattr(lib, name).restype = I

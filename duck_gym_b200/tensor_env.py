@@ -12,10 +12,10 @@ reference's generator calls, so it reproduces the reference env's draws on the
 same device.
 
 Supported: tasks "standing" and "locomotion", the velocity filter, fixed or
-random command directions, fp32 and fp64.  The gait reference, foot-clearance
-and load-transfer shaping need the MuJoCo-prepared ``gait.npz`` assets, which
-this build does not produce; requesting them raises.  There is no CPU backend:
-the CPU path of the reference is its own solver.
+random command directions, the gait reference, foot-clearance and
+load-transfer shaping (from the ``gait.npz`` next to the model, as in the
+reference), fp32 and fp64.  There is no CPU backend: the CPU path of the
+reference is its own solver.
 """
 
 from __future__ import annotations
@@ -35,7 +35,11 @@ class EnvParams(ctypes.Structure):
                 ("root_height", ctypes.c_double), ("tilt", ctypes.c_double), ("control_dt", ctypes.c_double),
                 ("velocity_alpha", ctypes.c_double), ("tracking_weight", ctypes.c_double),
                 ("heading_weight", ctypes.c_double), ("tracking_sigma", ctypes.c_double),
-                ("gait_period", ctypes.c_double), ("iquat", ctypes.c_double * 4)]
+                ("gait_period", ctypes.c_double), ("iquat", ctypes.c_double * 4),
+                ("gait", ctypes.c_int), ("foot_clearance", ctypes.c_int), ("load_transfer", ctypes.c_int),
+                ("gait_samples", ctypes.c_int), ("foot_points", ctypes.c_int), ("foot_body", ctypes.c_int * 2),
+                ("gait_lift", ctypes.c_double), ("mass", ctypes.c_double),
+                ("gait_table", ctypes.c_void_p), ("foot_xyz", ctypes.c_void_p)]
 
 
 def _ptr(t):
@@ -55,14 +59,17 @@ class TensorEnv:
             raise ValueError(backend)
         if backend != "cuda":
             raise ValueError("duck_gym_b200 runs on CUDA only; the CPU path is the reference's own solver")
-        if gait or foot_clearance or load_transfer:
-            raise NotImplementedError("gait, foot_clearance and load_transfer need the MuJoCo-prepared gait.npz")
         self.device = torch.device("cuda", device)
         self.num_envs = num_envs
         self.num_actions = 14
         self.dtype = torch.float64 if fp64 else torch.float32
         self.model_dir = Path(model_dir)
         self.meta = json.loads((self.model_dir / "metadata.json").read_text())
+        self._gait_record = None
+        if gait or foot_clearance or load_transfer:
+            import numpy as np
+
+            self._gait_record = np.load(self.model_dir / "gait.npz")
         self.native = CudaBatch(str(self.model_dir / "microduck.duck"), num_envs, dt, iterations, device, fp64)
         if self.native.joint_names != self.meta["joint_names"]:
             raise ValueError("Joint order mismatch")
@@ -87,12 +94,25 @@ class TensorEnv:
         self.substeps = substeps
         self.action_scale = action_scale
         self.max_episode_length = round(episode_seconds / self.control_dt)
-        self.gait = False
+        self.gait, self.foot_clearance, self.load_transfer = gait, foot_clearance, load_transfer
         self.gait_period = 0.8
-        self.tracking_sigma = tracking_sigma if tracking_sigma is not None else 0.04
+        self.tracking_sigma = tracking_sigma if tracking_sigma is not None else (0.02 if gait else 0.04)
         if self.tracking_sigma <= 0:
             raise ValueError("tracking sigma must be positive")
         self.command_speed = command_speed
+        if gait or foot_clearance or load_transfer:
+            # tensor_env.py:152-171: the gait record prepared next to the model.
+            record = self._gait_record
+            self.gait_table = torch.tensor(record["targets"], device=self.device, dtype=self.dtype).contiguous()
+            self.gait_period = float(record["period"])
+            self.gait_lift = float(record["lift"]) if "lift" in record.files else 0.008
+            self.foot_points = torch.tensor(record["foot_collision_points"], device=self.device,
+                                            dtype=self.dtype).contiguous()
+            self.foot_bodies = torch.tensor(record["foot_bodies"], device=self.device, dtype=torch.long)
+            if abs(float(record["speed"]) - command_speed) > 1e-8:
+                raise ValueError("Gait command speed mismatch")
+            self.gait_directions = torch.tensor([[1.0, 0], [-1, 0], [0, 1], [0, -1]], device=self.device,
+                                                dtype=self.dtype)
         self.direction_names = ("forward", "backward", "left", "right")
         if command_direction not in ("all", *self.direction_names):
             raise ValueError("Invalid command direction")
@@ -121,6 +141,13 @@ class TensorEnv:
             velocity_alpha=self.velocity_alpha, tracking_weight=tracking_weight, heading_weight=heading_weight,
             tracking_sigma=self.tracking_sigma, gait_period=self.gait_period,
             iquat=(ctypes.c_double * 4)(*[float(v) for v in self.iquat.cpu()]))
+        if gait or foot_clearance or load_transfer:
+            p = self._params
+            p.gait, p.foot_clearance, p.load_transfer = int(gait), int(foot_clearance), int(load_transfer)
+            p.gait_samples, p.foot_points = self.gait_table.shape[1], self.foot_points.shape[1]
+            p.foot_body = (ctypes.c_int * 2)(*[int(v) for v in self.foot_bodies.tolist()])
+            p.gait_lift, p.mass = self.gait_lift, float(self.meta["mass"])
+            p.gait_table, p.foot_xyz = self.gait_table.data_ptr(), self.foot_points.data_ptr()
         self._lib = library()
         self.num_obs = self._lib.duck_env_obs_dim(self.native._h, ctypes.byref(self._params))
         self.reset(torch.ones(num_envs, device=dev, dtype=torch.bool))
@@ -192,15 +219,33 @@ class TensorEnv:
         return self._observe(), {"observations": {}}
 
     def reference(self):
-        return self.home.expand(self.num_envs, -1)
+        """tensor_env.py:263-277 (torch ops; the step uses the fused kernel)."""
+        if not self.gait:
+            return self.home.expand(self.num_envs, -1)
+        phase = self.episode_length_buf.to(self.dtype) * self.control_dt / self.gait_period
+        count = self.gait_table.shape[1]
+        index = (phase % 1) * count
+        lo = index.long()
+        fraction = (index - lo)[:, None]
+        direction = (self.commands @ self.gait_directions.T).argmax(-1)
+        ref = (self.gait_table[direction, lo] * (1 - fraction)
+               + self.gait_table[direction, (lo + 1) % count] * fraction)
+        blend = (self.episode_length_buf.to(self.dtype) * self.control_dt).clamp(0, 1)[:, None]
+        return self.home + (ref - self.home) * blend
 
     def step(self, actions):
         """tensor_env.py:279-391."""
         lib, h, stream = self._lib, self.native._h, self._stream
         n = self.num_envs
         acts = actions.to(self.device, self.dtype).contiguous()
-        _raise(lib.duck_env_targets(h, _ptr(acts), float(self.action_scale), _ptr(self.home), _ptr(self.lower),
-                                    _ptr(self.upper), _ptr(self._a), _ptr(self._target), stream))
+        if self.gait:
+            _raise(lib.duck_env_reference_targets(
+                h, ctypes.byref(self._params), _ptr(acts), float(self.action_scale), _ptr(self.home),
+                _ptr(self.lower), _ptr(self.upper), _ptr(self.episode_length_buf), _ptr(self.commands),
+                _ptr(self._a), _ptr(self._target), stream))
+        else:
+            _raise(lib.duck_env_targets(h, _ptr(acts), float(self.action_scale), _ptr(self.home), _ptr(self.lower),
+                                        _ptr(self.upper), _ptr(self._a), _ptr(self._target), stream))
         self.native.step(self._target, self.forces, self.substeps, self.meta["kp"], self.meta["torque_limit"])
         obs = torch.empty(n, self.num_obs, device=self.device)
         reward = torch.empty(n, device=self.device)

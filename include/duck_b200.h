@@ -166,6 +166,15 @@ typedef struct duck_env_params {
   double root_height, tilt, control_dt, velocity_alpha, tracking_weight, heading_weight, tracking_sigma,
       gait_period;
   double iquat[4]; /* conjugated root principal-frame quaternion (w, x, y, z) */
+  /* Gait shaping from the env's gait.npz (tensor_env.py:152-171): the gait
+   * reference targets (gait), the foot-clearance and load-transfer rewards.
+   * gait_table [4 directions, gait_samples, J] and foot_xyz [2, foot_points, 3]
+   * (foot collision points in foot-body coordinates) are Real device arrays;
+   * mass is the robot's total mass. */
+  int gait, foot_clearance, load_transfer, gait_samples, foot_points;
+  int foot_body[2];
+  double gait_lift, mass;
+  const void *gait_table, *foot_xyz;
 } duck_env_params;
 
 /* Observation width of the environment described by params (52, 58 or 60 for
@@ -178,6 +187,16 @@ int duck_env_obs_dim(const duck_batch *batch, const duck_env_params *params);
 int duck_env_targets(duck_batch *batch, const void *actions, double scale, const void *home,
                      const void *lower, const void *upper, void *a_out, void *target_out,
                      duck_stream stream);
+
+/* tensor_env.py:263-283: a = clamp(actions, -1, 1), target = clamp(ref + scale a,
+ * lower, upper) where ref is HOME or, with params->gait, the gait table at the
+ * episode phase in the command's direction blended in over the first second.
+ * episode_length [E] int64 and commands [E,2] are the env buffers before the
+ * step. */
+int duck_env_reference_targets(duck_batch *batch, const duck_env_params *params, const void *actions,
+                               double scale, const void *home, const void *lower, const void *upper,
+                               const int64_t *episode_length, const void *commands, void *a_out,
+                               void *target_out, duck_stream stream);
 
 /* tensor_env.py:291-361 after the physics step: projected gravity and body
  * velocities, termination (failed), reward, time-outs, done, episode

@@ -51,10 +51,39 @@ class EnvConfig:
     tracking_sigma: float = 0.04
     gait_period: float = 0.8
     tilt: float | None = None   # -cos(0.5) as the env's device computes it; None: this CPU's
+    # Gait shaping (tensor_env.py:152-171, 263-277, 318-344), from gait.npz.
+    gait: bool = False
+    foot_clearance: bool = False
+    load_transfer: bool = False
+    gait_table: torch.Tensor | None = None     # [4, samples, J]
+    gait_lift: float = 0.008
+    foot_points: torch.Tensor | None = None    # [2, P, 3]
+    foot_bodies: list | None = None
+    mass: float = 0.0
 
     @property
     def iquat(self):   # tensor_env.py:137-139
         return torch.tensor(self.root_iquat, dtype=self.home.dtype) * torch.tensor([1, -1, -1, -1])
+
+
+def reference_targets(episode_length, commands, cfg: EnvConfig):
+    """tensor_env.py:263-277: HOME, or the gait table interpolated at the
+    episode phase in the command's direction, blended in over the first
+    second."""
+    n = episode_length.shape[0]
+    if not cfg.gait:
+        return cfg.home.expand(n, -1)
+    dt = cfg.home.dtype
+    directions = torch.tensor([[1.0, 0], [-1, 0], [0, 1], [0, -1]], dtype=dt)
+    phase = episode_length.to(dt) * cfg.control_dt / cfg.gait_period
+    count = cfg.gait_table.shape[1]
+    index = (phase % 1) * count
+    lo = index.long()
+    fraction = (index - lo)[:, None]
+    direction = (commands @ directions.T).argmax(-1)
+    ref = cfg.gait_table[direction, lo] * (1 - fraction) + cfg.gait_table[direction, (lo + 1) % count] * fraction
+    blend = (episode_length.to(dt) * cfg.control_dt).clamp(0, 1)[:, None]
+    return cfg.home + (ref - cfg.home) * blend
 
 
 def features(b, cfg: EnvConfig):
@@ -79,10 +108,12 @@ def observations(b, j, g, v, w, yaw, actions, episode_length, commands, filtered
     return torch.cat(pieces, dim=-1).float()
 
 
-def post_step(b, j, d, a, prev_actions, episode_length, returns, commands, filtered, cfg: EnvConfig):
+def post_step(b, j, d, a, prev_actions, episode_length, returns, commands, filtered, cfg: EnvConfig,
+              contact_forces=None):
     """tensor_env.py:291-361: everything ``step`` computes after the physics
     and before its auto-reset.  Returns a dict with obs (the terminal
-    observation), reward, failed, timeout, done and the updated buffers."""
+    observation), reward, failed, timeout, done and the updated buffers.
+    ``contact_forces`` [E,B,3] (all contacts) feeds the load-transfer term."""
     g, v, w, yaw = features(b, cfg)
     height = b[:, 1, 2] - cfg.root_height
     tilt = -torch.cos(torch.tensor(0.5)) if cfg.tilt is None else torch.tensor(cfg.tilt)
@@ -104,6 +135,22 @@ def post_step(b, j, d, a, prev_actions, episode_length, returns, commands, filte
                   + cfg.tracking_weight * torch.exp(-error / cfg.tracking_sigma ** 2)
                   - 0.1 * w.square().sum(-1) - cfg.heading_weight * (1 - yaw[:, 0])
                   - 0.02 * a.square().sum(-1) - 0.03 * (a - prev_actions).square().sum(-1))
+    if cfg.foot_clearance:   # tensor_env.py:318-333
+        poses = b[:, cfg.foot_bodies]
+        up = torch.tensor([0.0, 0, 1.0], dtype=b.dtype).expand(b.shape[0], 2, -1)
+        local_up = inverse_rotate(poses[:, :, 3:7], up)
+        heights = torch.einsum("fvi,efi->efv", cfg.foot_points, local_up) + poses[:, :, None, 2]
+        clearance = heights.amin(-1)
+        phase = ((episode_length[:, None] + 1) * cfg.control_dt / cfg.gait_period + torch.tensor([0.0, 0.5])) % 1
+        swing = ((phase - 0.6) / 0.4).clamp(0, 1)
+        desired = cfg.gait_lift * torch.sin(torch.pi * swing).square()
+        reward -= 20000 * (clearance.clamp_min(0) - desired).square().sum(-1)
+    if cfg.load_transfer:    # tensor_env.py:334-344
+        forces = contact_forces[:, cfg.foot_bodies, 2].to(b.dtype) / (cfg.mass * 9.81)
+        cycle = (episode_length.to(b.dtype) + 1) * cfg.control_dt / cfg.gait_period
+        left = 0.5 + 0.5 * torch.sin(2 * torch.pi * (cycle - 0.05))
+        wanted = torch.stack((left, 1 - left), dim=-1)
+        reward -= 3 * (forces.clamp(0, 3) - wanted).square().sum(-1)
     reward = torch.where(failed, -2.0, reward) * cfg.control_dt
     episode_length = episode_length + 1
     returns = returns + reward.float()
@@ -114,13 +161,29 @@ def post_step(b, j, d, a, prev_actions, episode_length, returns, commands, filte
                 episode_length=episode_length, returns=returns, filtered=filtered, actions=a)
 
 
-def config_from_fixture(config: dict, metadata: dict, dtype=torch.float32) -> EnvConfig:
-    return EnvConfig(
+def config_from_fixture(config: dict, metadata: dict, dtype=torch.float32, gait_record=None) -> EnvConfig:
+    cfg = EnvConfig(
         task=config["task"], home=torch.tensor(metadata["home"], dtype=dtype), root_height=metadata["root_height"],
         root_iquat=metadata["root_iquat"], control_dt=config["control_dt"],
         max_episode_length=config["max_episode_length"], velocity_filter_seconds=config["velocity_filter_seconds"],
         velocity_alpha=config["velocity_alpha"], tracking_weight=config["tracking_weight"],
         heading_weight=config["heading_weight"], tracking_sigma=config["tracking_sigma"])
+    if config.get("gait"):
+        apply_gait(cfg, gait_record, metadata, True, True, True)
+    return cfg
+
+
+def apply_gait(cfg: EnvConfig, record, metadata, gait, foot_clearance, load_transfer):
+    """tensor_env.py:152-171: the gait.npz fields the shaping reads."""
+    dt = cfg.home.dtype
+    cfg.gait, cfg.foot_clearance, cfg.load_transfer = gait, foot_clearance, load_transfer
+    cfg.gait_table = torch.tensor(record["targets"], dtype=dt)
+    cfg.gait_period = float(record["period"])
+    cfg.gait_lift = float(record["lift"]) if "lift" in record else 0.008
+    cfg.foot_points = torch.tensor(record["foot_collision_points"], dtype=dt)
+    cfg.foot_bodies = [int(v) for v in record["foot_bodies"]]
+    cfg.mass = float(metadata["mass"])
+    return cfg
 
 
 __all__ = ["EnvConfig", "features", "observations", "post_step", "multiply", "inverse_rotate", "config_from_fixture",

@@ -41,12 +41,25 @@ def make_env(biped_dir, **kw):
 
 
 def env_config(env):
-    return env_math.EnvConfig(
+    cfg = env_math.EnvConfig(
         task=env.task, home=env.home.cpu(), root_height=env.meta["root_height"], root_iquat=env.meta["root_iquat"],
         control_dt=env.control_dt, max_episode_length=env.max_episode_length,
         velocity_filter_seconds=env.velocity_filter_seconds, velocity_alpha=env.velocity_alpha,
         tracking_weight=env.tracking_weight, heading_weight=env.heading_weight, tracking_sigma=env.tracking_sigma,
         tilt=env._params.tilt)
+    if env._gait_record is not None:
+        env_math.apply_gait(cfg, env._gait_record, env.meta, env.gait, env.foot_clearance, env.load_transfer)
+    return cfg
+
+
+@pytest.fixture(scope="module")
+def gait_dir(tmp_path_factory):
+    from duck_gym_b200 import biped
+
+    d = tmp_path_factory.mktemp("gait")
+    biped.write(d, seed=0)
+    biped.write_gait(d, seed=0)
+    return d
 
 
 def snapshot(env):
@@ -56,9 +69,14 @@ def snapshot(env):
 
 def check_step(env, cfg, before, actions, obs, reward, done, info, tol):
     b, j, d = [t.cpu() for t in env.native.state()]
+    forces = env.native.contact_forces().cpu()
     a = actions.to(env.dtype).clamp(-1, 1)
     ref = env_math.post_step(b, j, d, a, before["actions"], before["episode_length_buf"], before["returns"],
-                             before["commands"], before["filtered_velocity"], cfg)
+                             before["commands"], before["filtered_velocity"], cfg, contact_forces=forces)
+    if cfg.gait:
+        want = (env_math.reference_targets(before["episode_length_buf"], before["commands"], cfg)
+                + env.action_scale * a).clamp(env.lower.cpu(), env.upper.cpu())
+        torch.testing.assert_close(info["applied_targets"].cpu(), want, **tol["obs"])
     for key, got in (("failed", info["failed"]), ("timeout", info["time_outs"]), ("done", done)):
         assert torch.equal(got.cpu(), ref[key]), key
     assert torch.equal(env.episode_length_buf.cpu(), ref["episode_length"])
@@ -72,14 +90,16 @@ def check_step(env, cfg, before, actions, obs, reward, done, info, tol):
     return ref
 
 
-@pytest.mark.parametrize("task,filter_s,scale,fp64", [
-    ("standing", 0.0, 0.3, False),
-    ("locomotion", 0.8, 0.6, False),
-    ("locomotion", 0.0, 0.6, True),
+@pytest.mark.parametrize("task,filter_s,scale,fp64,gait", [
+    ("standing", 0.0, 0.3, False, False),
+    ("locomotion", 0.8, 0.6, False, False),
+    ("locomotion", 0.0, 0.6, True, False),
+    ("locomotion", 0.0, 0.6, False, True),
 ])
-def test_fused_step_matches_env_math(biped_dir, task, filter_s, scale, fp64):
-    env = make_env(biped_dir, task=task, velocity_filter_seconds=filter_s, action_scale=scale,
-                   episode_seconds=0.3, fp64=fp64, auto_reset=False)
+def test_fused_step_matches_env_math(biped_dir, gait_dir, task, filter_s, scale, fp64, gait):
+    env = make_env(gait_dir if gait else biped_dir, task=task, velocity_filter_seconds=filter_s, action_scale=scale,
+                   episode_seconds=0.3, fp64=fp64, auto_reset=False, gait=gait, foot_clearance=gait,
+                   load_transfer=gait)
     cfg = env_config(env)
     tol = ({"obs": FP64_TOL, "reward": dict(rtol=1e-12, atol=1e-13)} if fp64 else
            {"obs": OBS_TOL, "reward": REWARD_TOL})
@@ -114,6 +134,32 @@ def records_from_golden(bodies, diag, record_length):
     body[:, :, :13] = bodies
     rec[:, 8:8 + 16 * B] = body.reshape(E, -1)
     return rec
+
+
+def test_gait_targets_on_reference_states(gait_dir):
+    """The reference env's recorded applied targets (gait table, blend,
+    clamp) from the recorded buffers, through duck_env_reference_targets."""
+    from duck_gym_b200 import cuda_batch
+    from duck_gym_b200.tensor_env import _ptr
+    import ctypes
+
+    g = np.load(GOLDEN / "env_gait.npz")
+    config = ast.literal_eval(str(g["config"]))
+    env = make_env(gait_dir, num_envs=6, task="locomotion", episode_seconds=config["episode_seconds"],
+                   action_scale=config["action_scale"], auto_reset=False, gait=True, foot_clearance=True,
+                   load_transfer=True)
+    np.testing.assert_array_equal(env.gait_table.cpu().numpy(), g["gait_targets"].astype(np.float32))
+    lib = cuda_batch.library()
+    for i in range(g["actions"].shape[0]):
+        cuda_t = lambda name, dtype=torch.float32: torch.from_numpy(np.ascontiguousarray(g[name][i])).cuda().to(dtype)
+        a_out, target = torch.empty(6, 14, device="cuda"), torch.empty(6, 14, device="cuda")
+        # Inputs bound to names: a temporary's memory could be reused before the launch.
+        actions, length, commands = cuda_t("actions"), cuda_t("episode_length", torch.int64), cuda_t("commands")
+        cuda_batch._raise(lib.duck_env_reference_targets(
+            env.native._h, ctypes.byref(env._params), _ptr(actions), float(config["action_scale"]),
+            _ptr(env.home), _ptr(env.lower), _ptr(env.upper), _ptr(length), _ptr(commands), _ptr(a_out),
+            _ptr(target), env._stream))
+        np.testing.assert_allclose(target.cpu().numpy(), g["applied_targets"][i], rtol=0, atol=1e-6)
 
 
 @pytest.mark.parametrize("case", ["env_standing", "env_locomotion"])
