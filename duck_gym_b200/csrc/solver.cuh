@@ -355,29 +355,44 @@ template <class R, int T> struct Solver {
     // larger point sets recompute them per pick.  Either way every point is
     // evaluated with the same arithmetic, so the picks are identical.
     if (count <= 8) {
+      // The candidates still open for a pick: below 3 mm and 5 mm or more
+      // (laterally) from every earlier pick.  After each pick the distance test
+      // runs for all candidates at once (independent, so it pipelines) instead
+      // of inside the scan; the scan keeps the reference's order and
+      // comparisons (first candidate not above the running minimum), NaN
+      // heights included, so the picks are the same.
       V3<R> wps[8];
       R zs[8];
+      unsigned open = 0u;
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        if (k < count) zs[k] = pickPoint(s, k, x, v, w, q, dt, dt2, accel, wps[k]);
-      for (int pick = 0; pick < 4; ++pick) {
+        if (k < count) {
+          zs[k] = pickPoint(s, k, x, v, w, q, dt, dt2, accel, wps[k]);
+          if (!(double(zs[k]) >= .003)) open |= 1u << k;
+        }
+      for (int pick = 0; pick < 4 && open; ++pick) {
         int best = -1;
         R lowest = R(INFINITY);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if ((open >> k & 1u) && !(zs[k] >= lowest)) {
+            best = k;
+            lowest = zs[k];
+          }
+        if (best < 0) break;
         V3<R> bestWorld{};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          if (k >= count) continue;
-          const R z = zs[k];
-          if (double(z) >= .003 || z >= lowest || !pickApart(wps[k], world, n)) continue;
-          best = k;
-          lowest = z;
-          bestWorld = wps[k];
-        }
-        if (best < 0) break;
+        for (int k = 0; k < 8; ++k)
+          if (k == best) bestWorld = wps[k];
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           if (c == n) { feature[c] = best; world[c] = bestWorld; }
         ++n;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if ((open >> k & 1u) &&
+              double(xhypot(xsub(bestWorld.x, wps[k].x), xsub(bestWorld.y, wps[k].y))) < .005)
+            open &= ~(1u << k);
       }
       return n;
     }
