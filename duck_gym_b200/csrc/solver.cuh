@@ -877,19 +877,30 @@ template <class R, int T> struct Solver {
     // Contacts touching bi, in list order.
     const int nGround = I[iGround];
     const SV Rb = rot(bi);
-    if (L.cap <= 64) {
-      unsigned long long mask = unsigned(I[L.masks + 2 * bi]) | (unsigned long long)unsigned(I[L.masks + 2 * bi + 1]) << 32;
-      while (mask) {
-        const int ci = __ffsll((long long)mask) - 1;
+    // One loop (one inlined copy of the contact rows) over the contacts that
+    // touch bi, in list order: from the per-body bit mask when the list fits
+    // 64 entries, else by scanning the list.
+    const bool useMask = L.cap <= 64;
+    unsigned long long mask =
+        useMask ? unsigned(I[L.masks + 2 * bi]) | (unsigned long long)unsigned(I[L.masks + 2 * bi + 1]) << 32 : 0ull;
+    const int count = useMask ? 0 : I[iCount];
+    int scan = 0;
+    for (;;) {
+      int ci = -1;
+      if (useMask) {
+        if (!mask) break;
+        ci = __ffsll((long long)mask) - 1;
         mask &= mask - 1;
-        if (mine()) stampContact(bi, ci, x, Rb, nGround, H, g);
+      } else {
+        while (scan < count) {
+          const int meta = cmeta(scan);
+          if (metaBody(meta) == bi || metaOther(meta) == bi) break;
+          ++scan;
+        }
+        if (scan >= count) break;
+        ci = scan++;
       }
-    } else {
-      const int n = I[iCount];
-      for (int ci = 0; ci < n; ++ci) {
-        const int meta = cmeta(ci);
-        if ((metaBody(meta) == bi || metaOther(meta) == bi) && mine()) stampContact(bi, ci, x, Rb, nGround, H, g);
-      }
+      if (mine()) stampContact(bi, ci, x, Rb, nGround, H, g);
     }
     if constexpr (kSplit == 2) {
       const unsigned pair = 3u << ((threadIdx.x & 31) & ~1);
