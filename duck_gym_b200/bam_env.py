@@ -65,7 +65,7 @@ BUFFER_NAMES = ("home", "root_offset", "zero_forces", "action", "old_action", "p
                 "observed_velocity", "command", "mean_velocity_world", "target_yaw", "self_contacts",
                 "self_penetration", "air_time", "contact_time", "peak_height", "contact_force", "joints", "head_ema",
                 "target_history", "motor", "features", "terms", "contact", "history_initialized", "done", "timeout",
-                "failed", "episode_length", "counters", "obs_actor", "obs_critic", "reward")
+                "failed", "episode_length", "counters", "obs_actor", "obs_critic", "reward", "servo_supply")
 
 
 class BamBufferTable(ctypes.Structure):
@@ -205,6 +205,7 @@ class BamEnv:
         self._terms = zeros(E, len(TERM_NAMES))
         self._done, self._timeout, self._failed = (zeros(E, dtype=torch.bool) for _ in range(3))
         self._counters = torch.zeros(2, device=self.device, dtype=torch.int32)
+        self._servo_supply = zeros(E)
         self._obs_actor = torch.zeros(E, 19 + 3 * J, device=self.device)
         self._reward = torch.zeros(E, device=self.device)
         self._actions_in = zeros(E, J)
@@ -229,7 +230,7 @@ class BamEnv:
                "features": self._features, "terms": self._terms, "done": self._done, "timeout": self._timeout,
                "failed": self._failed, "counters": self._counters, "obs_actor": self._obs_actor,
                "obs_critic": getattr(self, "_obs_critic", None), "reward": self._reward,
-               "head_ema": self._head_ema, "peak_height": self._peak_height}
+               "head_ema": self._head_ema, "peak_height": self._peak_height, "servo_supply": self._servo_supply}
         t = own[name] if name in own else getattr(self, name)
         assert t.is_contiguous() and t.device == self.device
         return t

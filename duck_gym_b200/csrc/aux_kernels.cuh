@@ -213,29 +213,44 @@ __device__ __forceinline__ V3<R> envBodyForce(const DevModel<R> *m, const R *rec
   return f;
 }
 
+// Storage of the six per-body RNEA arrays (acceleration, angular
+// acceleration, force, moment, contact force, contact moment) in shared
+// memory, laid out [array][component][body][lane] so that the lanes of a warp
+// (one environment each) hit distinct banks.
+template <class R> struct RneaShared {
+  R *base;
+  int nb, lanes, lane;
+  __device__ __forceinline__ R &at(int a, int c, int b) const { return base[((a * 3 + c) * nb + b) * lanes + lane]; }
+  __device__ __forceinline__ V3<R> get(int a, int b) const { return {at(a, 0, b), at(a, 1, b), at(a, 2, b)}; }
+  __device__ __forceinline__ void set(int a, int b, V3<R> x) { at(a, 0, b) = x.x; at(a, 1, b) = x.y; at(a, 2, b) = x.z; }
+};
+enum { rAcc, rAlpha, rForce, rMoment, rContact, rContactMoment };
+
 // BasicState::generalizedLoads (kernel.cuh:504-554): RNEA at zero joint
 // acceleration for one environment; out [J,3] = (bias, contact + limit,
 // applied actuator) per hinge.
-template <class R>
-__device__ __noinline__ void envGeneralizedLoads(const DevModel<R> *__restrict__ m, const R *rec, V3<R> off,
-                                                 R *o, const R *envMass = nullptr, const R *envInertia = nullptr) {
+template <class R, class Store>
+__device__ __forceinline__ void rneaLoads(const DevModel<R> *__restrict__ m, const R *rec, V3<R> off, R *o,
+                                          const R *envMass, const R *envInertia, Store &st) {
   const int nb = m->nb, nj = m->nj;
   const R *bodies = rec + kRecHeader;
   const R *joints = bodies + kRecBody * nb;
-  V3<R> acc[kMaxBodies], alpha[kMaxBodies], force[kMaxBodies], moment[kMaxBodies], contact[kMaxBodies],
-      contactMoment[kMaxBodies];
   const V3<R> zero{R(0), R(0), R(0)};
-  for (int b = 0; b < nb; ++b) acc[b] = alpha[b] = force[b] = moment[b] = contact[b] = contactMoment[b] = zero;
+  for (int b = 0; b < nb; ++b)
+    for (int a = 0; a < 6; ++a) st.set(a, b, zero);
   auto X = [&](int b) { return gv3(bodies + kRecBody * b); };
   auto Q = [&](int b) { return gq4(bodies + kRecBody * b + 3); };
   auto W = [&](int b) { return gv3(bodies + kRecBody * b + 10); };
-  acc[1] = cross(W(1), cross(W(1), rotate(Q(1), off)));
+  st.set(rAcc, 1, cross(W(1), cross(W(1), rotate(Q(1), off))));
   for (int j = 0; j < nj; ++j) {
     const int a = __ldg(&m->ja[j]), b = __ldg(&m->jb[j]);
     V3<R> axis = rotate(Q(a), mvec(m->axisA[j])), ra = rotate(Q(a), mvec(m->ra[j])), rb = rotate(Q(b), mvec(m->rb[j]));
     R speed = dot(W(b) - W(a), axis);
-    alpha[b] = alpha[a] + cross(W(a), axis) * speed;
-    acc[b] = acc[a] + cross(alpha[a], ra) + cross(W(a), cross(W(a), ra)) - cross(alpha[b], rb) - cross(W(b), cross(W(b), rb));
+    const V3<R> alphaA = st.get(rAlpha, a), accA = st.get(rAcc, a);
+    const V3<R> alphaB = alphaA + cross(W(a), axis) * speed;
+    st.set(rAlpha, b, alphaB);
+    st.set(rAcc, b, accA + cross(alphaA, ra) + cross(W(a), cross(W(a), ra)) - cross(alphaB, rb) -
+                        cross(W(b), cross(W(b), rb)));
   }
   const V3<R> gravity{m->gravity[0], m->gravity[1], m->gravity[2]};
   for (int i = 1; i < nb; ++i) {
@@ -249,8 +264,8 @@ __device__ __noinline__ void envGeneralizedLoads(const DevModel<R> *__restrict__
       V3<R> l = rotateInv(q, v);
       return rotate(q, V3<R>{l.x * in.x, l.y * in.y, l.z * in.z});
     };
-    force[i] = (acc[i] - gravity) * mass;
-    moment[i] = inertiaMul(alpha[i]) + cross(W(i), inertiaMul(W(i)));
+    st.set(rForce, i, (st.get(rAcc, i) - gravity) * mass);
+    st.set(rMoment, i, inertiaMul(st.get(rAlpha, i)) + cross(W(i), inertiaMul(W(i))));
   }
   const R *cs = recContacts(m, rec);
   const int n = int(rec[1]);
@@ -258,42 +273,50 @@ __device__ __noinline__ void envGeneralizedLoads(const DevModel<R> *__restrict__
     const R *c = cs + kRecContact * i;
     const int body = int(c[0]), other = int(c[3]);
     V3<R> f = -recContactWorld(c, V3<R>{c[26], c[27], c[28]});
-    contact[body] = contact[body] + f;
-    contactMoment[body] = contactMoment[body] + cross(rotate(Q(body), V3<R>{c[6], c[7], c[8]}), f);
+    st.set(rContact, body, st.get(rContact, body) + f);
+    st.set(rContactMoment, body, st.get(rContactMoment, body) + cross(rotate(Q(body), V3<R>{c[6], c[7], c[8]}), f));
     if (other >= 0) {
-      contact[other] = contact[other] - f;
-      contactMoment[other] = contactMoment[other] + cross(rotate(Q(other), V3<R>{c[12], c[13], c[14]}), -f);
+      st.set(rContact, other, st.get(rContact, other) - f);
+      st.set(rContactMoment, other,
+             st.get(rContactMoment, other) + cross(rotate(Q(other), V3<R>{c[12], c[13], c[14]}), -f));
     }
   }
   for (int k = nj - 1; k >= 0; --k) {
     const int a = __ldg(&m->ja[k]), b = __ldg(&m->jb[k]);
     const R *jr = joints + kRecJoint * k;
     V3<R> axis = rotate(Q(a), mvec(m->axisA[k])), rb = rotate(Q(b), mvec(m->rb[k])), shift = X(b) - X(a);
-    o[3 * k] = dot(axis, moment[b] - cross(rb, force[b]));
-    o[3 * k + 1] = dot(axis, contactMoment[b] - cross(rb, contact[b])) +
+    const V3<R> forceB = st.get(rForce, b), momentB = st.get(rMoment, b);
+    const V3<R> contactB = st.get(rContact, b), contactMomentB = st.get(rContactMoment, b);
+    o[3 * k] = dot(axis, momentB - cross(rb, forceB));
+    o[3 * k + 1] = dot(axis, contactMomentB - cross(rb, contactB)) +
                    (__ldg(&m->limited[k]) ? -jr[5] + jr[6] : R(0));
     R angle, rate;
     jointState(m, bodies, k, &angle, &rate);
     const R kp = jr[17], maxTorque = jr[18];
     R motor = jr[19] - kp * wrapAngle(angle - jr[16]);
     o[3 * k + 2] = maxTorque > R(0) ? rclamp(motor, -maxTorque, maxTorque) : motor;
-    moment[a] = moment[a] + (moment[b] + cross(shift, force[b]));
-    force[a] = force[a] + force[b];
-    contactMoment[a] = contactMoment[a] + (contactMoment[b] + cross(shift, contact[b]));
-    contact[a] = contact[a] + contact[b];
+    st.set(rMoment, a, st.get(rMoment, a) + (momentB + cross(shift, forceB)));
+    st.set(rForce, a, st.get(rForce, a) + forceB);
+    st.set(rContactMoment, a, st.get(rContactMoment, a) + (contactMomentB + cross(shift, contactB)));
+    st.set(rContact, a, st.get(rContact, a) + contactB);
   }
 }
 
-// BasicState::generalizedLoads (kernel.cuh:504-554), one thread per environment.
+
+// BasicState::generalizedLoads (kernel.cuh:504-554), one thread per
+// environment, 32 per block, the RNEA arrays in shared memory
+// (18 x B x 32 Reals per block).
 template <class R>
 __global__ void generalizedLoadsKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
                                        const R *offset, R *out, const R *envMass, const R *envInertia) {
+  extern __shared__ __align__(16) unsigned char loadsRaw[];
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= count) return;
   const R *off = offset + 3 * size_t(e);
-  envGeneralizedLoads(m, records + size_t(e) * stride, V3<R>{off[0], off[1], off[2]}, out + size_t(e) * m->nj * 3,
-                      envMass ? envMass + size_t(e) * m->nb : nullptr,
-                      envInertia ? envInertia + size_t(e) * m->nb * 3 : nullptr);
+  RneaShared<R> st{reinterpret_cast<R *>(loadsRaw), m->nb, int(blockDim.x), int(threadIdx.x)};
+  rneaLoads(m, records + size_t(e) * stride, V3<R>{off[0], off[1], off[2]}, out + size_t(e) * m->nj * 3,
+            envMass ? envMass + size_t(e) * m->nb : nullptr, envInertia ? envInertia + size_t(e) * m->nb * 3 : nullptr,
+            st);
 }
 
 // Per-environment parameter check: a non-finite or non-positive mass or

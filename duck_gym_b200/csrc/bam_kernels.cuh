@@ -5,8 +5,10 @@
 //
 //   bamBeginKernel      step prologue: action history, observed velocity,
 //                       self-contact maxima cleared, step counter  (:292-303)
-//   bamServoKernel      delay ring, RNEA generalized loads and the XL330/m6
-//                       servo -> motor channels for one substep   (:305-331)
+//   bamLoadsKernel      RNEA generalized loads (shared-memory arrays) and
+//                       the servo's supply voltage                (:305-314)
+//   bamServoJointKernel delay ring and the XL330/m6 servo, one thread per
+//                       (env, joint) -> motor channels            (:305-331)
 //   (physics: advanceMotor of duck_b200.cu, one substep)
 //   bamAfterKernel      foot contacts, air / contact timers, self-contact
 //                       maxima, mean-velocity filter, ring cursor (:332-344)
@@ -56,7 +58,7 @@ template <class R> struct BamBuffers {
   const R *home, *rootOffset;
   R *action, *oldAction, *prevMotor, *prevApplied, *observedVelocity, *command, *meanVelocity, *targetYaw;
   R *airTime, *contactTime, *contactForce, *selfContacts, *selfPenetration, *joints, *headEma, *peakHeight;
-  R *history, *motor, *features, *terms;
+  R *history, *motor, *features, *terms, *servoSupply;
   bool *contact, *histInit, *done, *timeout, *failed;
   long long *episodeLength;
   int *counters;  // [0] delay-ring cursor, [1] common step counter
@@ -90,59 +92,72 @@ __global__ void bamBeginKernel(BamKernelParams p, BamBuffers<R> B, int count, co
 }
 
 // ---------------------------------------------------------------- servo
-// actuator.py:16-77 for one environment and every joint; writes the motor
-// channels and the servo history.
+// actuator.py:16-77 in two kernels.  bamLoadsKernel: one thread per
+// environment, 32 per block, RNEA loads with their per-body arrays in shared
+// memory; the hinge loads go to the motor-channel buffer (scratch until the
+// joint kernel overwrites it) and the supply voltage to servoSupply.
+// bamServoJointKernel: one thread per (environment, joint): delay ring and
+// the servo equations, writing the motor channels and the servo history.
 template <class R>
-__global__ void bamServoKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
+__global__ void bamLoadsKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
                                BamKernelParams p, BamBuffers<R> B) {
+  extern __shared__ __align__(16) unsigned char rneaRaw[];
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= count) return;
-  const int nj = p.nj, slots = p.lag + 1;
-  const R *rec = records + size_t(e) * stride;
-  const R *bodies = rec + kRecHeader;
+  const int nj = p.nj;
+  RneaShared<R> st{reinterpret_cast<R *>(rneaRaw), m->nb, int(blockDim.x), int(threadIdx.x)};
+  const R *off = B.rootOffset + 3 * size_t(e);
+  rneaLoads(m, records + size_t(e) * stride, V3<R>{off[0], off[1], off[2]}, B.motor + size_t(e) * nj * 3,
+            B.envMass ? B.envMass + size_t(e) * m->nb : nullptr,
+            B.envInertia ? B.envInertia + size_t(e) * m->nb * 3 : nullptr, st);
+  R sumAbs = R(0);
+  for (int j = 0; j < nj; ++j) sumAbs += fabs(B.prevMotor[size_t(e) * nj + j]);
+  B.servoSupply[e] = rmax(R(p.vin) - R(p.vinDrop) * sumAbs, R(p.vinMin));
+}
+
+template <class R>
+__global__ void bamServoJointKernel(const DevModel<R> *__restrict__ m, const R *records, int stride, int count,
+                                    BamKernelParams p, BamBuffers<R> B) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int nj = p.nj;
+  if (t >= count * nj) return;
+  const int e = t / nj, j = t % nj;
+  const int slots = p.lag + 1;
+  const R *bodies = records + size_t(e) * stride + kRecHeader;
   const int cursor = B.counters[0];
   const int delayedSlot = ((cursor - p.lag) % slots + slots) % slots;
   const size_t plane = size_t(count) * nj;
-  const bool init = B.histInit[e];
-  R loads[3 * kMaxJoints];
-  const R *off = B.rootOffset + 3 * size_t(e);
-  envGeneralizedLoads(m, rec, V3<R>{off[0], off[1], off[2]}, loads, B.envMass ? B.envMass + size_t(e) * m->nb : nullptr,
-                      B.envInertia ? B.envInertia + size_t(e) * m->nb * 3 : nullptr);
-  R sumAbs = R(0);
-  for (int j = 0; j < nj; ++j) sumAbs += fabs(B.prevMotor[size_t(e) * nj + j]);
-  const R supply = rmax(R(p.vin) - R(p.vinDrop) * sumAbs, R(p.vinMin));
+  const size_t i = size_t(e) * nj + j;
+  const R target = B.home[i] + B.action[i];
+  B.history[size_t(cursor) * plane + i] = target;
+  if (!B.histInit[e])
+    for (int s = 0; s < slots; ++s) B.history[size_t(s) * plane + i] = target;
+  const R delayed = B.history[size_t(delayedSlot) * plane + i];
+  R *mo = B.motor + 3 * i;
+  const R ext = -mo[0] + mo[1];
+  const R supply = B.servoSupply[e];
   const R kt = R(p.kt), res = R(p.res);
   const R gain = R((4096 / (2 * 3.14159265358979323846)) / (256 * 885));
-  for (int j = 0; j < nj; ++j) {
-    const size_t i = size_t(e) * nj + j;
-    const R target = B.home[i] + B.action[i];
-    B.history[size_t(cursor) * plane + i] = target;
-    if (!init)
-      for (int s = 0; s < slots; ++s) B.history[size_t(s) * plane + i] = target;
-    const R delayed = B.history[size_t(delayedSlot) * plane + i];
-    R position, velocity;
-    jointState(m, bodies, j, &position, &velocity);
-    const R speed = velocity;
-    R duty = (delayed - position) * R(p.kpFw) * gain;
-    const R center = kt * speed / supply;
-    const R span = R(p.res * 1.75) / supply;
-    duty = rmin(rmax(duty, center - span), center + span);
-    duty = rmin(rmax(duty, R(-1)), R(1));
-    const R raw = kt * supply * duty / res - R(p.kt * p.kt) * speed / res;
-    const R stribeck = exp(-pow(fabs(velocity) / R(p.dthetaStribeck), R(p.alpha)));
-    const R mot = B.prevApplied[i], ext = -loads[3 * j] + loads[3 * j + 1];
-    const R quad = fabs(mot) > fabs(ext) ? R(p.lfeq) * (ext * ext) : R(p.lfmq) * (mot * mot);
-    const R budget = R(p.fBase) + stribeck * R(p.fStribeck) + fabs(ext * R(p.lfe) - mot * R(p.lfm)) +
-                     stribeck * fabs(ext * R(p.lfes) - mot * R(p.lfms)) + stribeck * quad;
-    const R applied = rmin(rmax(raw, R(-p.forceLimit)), R(p.forceLimit));
-    R *mo = B.motor + 3 * i;
-    mo[0] = applied;
-    mo[1] = budget;
-    mo[2] = R(p.fViscous);
-    B.prevMotor[i] = raw;
-    B.prevApplied[i] = applied;
-  }
-  B.histInit[e] = true;
+  R position, velocity;
+  jointState(m, bodies, j, &position, &velocity);
+  const R speed = velocity;
+  R duty = (delayed - position) * R(p.kpFw) * gain;
+  const R center = kt * speed / supply;
+  const R span = R(p.res * 1.75) / supply;
+  duty = rmin(rmax(duty, center - span), center + span);
+  duty = rmin(rmax(duty, R(-1)), R(1));
+  const R raw = kt * supply * duty / res - R(p.kt * p.kt) * speed / res;
+  const R stribeck = exp(-pow(fabs(velocity) / R(p.dthetaStribeck), R(p.alpha)));
+  const R mot = B.prevApplied[i];
+  const R quad = fabs(mot) > fabs(ext) ? R(p.lfeq) * (ext * ext) : R(p.lfmq) * (mot * mot);
+  const R budget = R(p.fBase) + stribeck * R(p.fStribeck) + fabs(ext * R(p.lfe) - mot * R(p.lfm)) +
+                   stribeck * fabs(ext * R(p.lfes) - mot * R(p.lfms)) + stribeck * quad;
+  const R applied = rmin(rmax(raw, R(-p.forceLimit)), R(p.forceLimit));
+  mo[0] = applied;
+  mo[1] = budget;
+  mo[2] = R(p.fViscous);
+  B.prevMotor[i] = raw;
+  B.prevApplied[i] = applied;
 }
 
 // ---------------------------------------------------------------- frames
@@ -214,6 +229,7 @@ __global__ void bamAfterKernel(const DevModel<R> *__restrict__ m, const R *recor
     B.joints[(size_t(e) * p.nj + j) * 2] = angle;
     B.joints[(size_t(e) * p.nj + j) * 2 + 1] = rate;
   }
+  B.histInit[e] = true;   // the servo has filled this env's delay ring
   if (e == 0) B.counters[0] = (B.counters[0] + 1) % (p.lag + 1);
 }
 

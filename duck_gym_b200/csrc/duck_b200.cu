@@ -209,7 +209,15 @@ template <class R> void statsLaunch(duck_batch *b, void *counts, void *self, cud
   ++b->launches;
 }
 template <class R> void loadsLaunch(duck_batch *b, const void *offset, void *out, cudaStream_t s) {
-  generalizedLoadsKernel<R><<<blocksFor(b->n, 64), 64, 0, s>>>(
+  static int limit[2][64] = {};
+  const int need = int(18 * b->nb * 32 * sizeof(R));
+  int &have = limit[sizeof(R) == 8][b->device & 63];
+  if (need > have) {
+    check(cudaFuncSetAttribute(generalizedLoadsKernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, need),
+          "cudaFuncSetAttribute");
+    have = need;
+  }
+  generalizedLoadsKernel<R><<<blocksFor(b->n, 32), 32, need, s>>>(
       static_cast<const DevModel<R> *>(b->devModel), static_cast<const R *>(b->records), b->recordStride, b->n,
       static_cast<const R *>(offset), static_cast<R *>(out), static_cast<const R *>(b->envMass),
       static_cast<const R *>(b->envInertia));
@@ -797,7 +805,8 @@ template <class R> BamBuffers<R> bamBuffers(const duck_bam_buffers *x) {
                         x->target_yaw, x->self_contacts, x->self_penetration, x->air_time, x->contact_time,
                         x->peak_height, x->contact_force, x->joints, x->head_ema, x->target_history, x->motor,
                         x->features, x->terms, x->contact, x->history_initialized, x->done, x->timeout,
-                        x->failed, x->episode_length, x->counters, x->obs_actor, x->obs_critic, x->reward};
+                        x->failed, x->episode_length, x->counters, x->obs_actor, x->obs_critic, x->reward,
+                        x->servo_supply};
   for (const void *ptr : need) require(ptr != nullptr, "Missing BAM buffer");
   BamBuffers<R> B;
   B.home = static_cast<const R *>(x->home);
@@ -822,6 +831,7 @@ template <class R> BamBuffers<R> bamBuffers(const duck_bam_buffers *x) {
   B.motor = static_cast<R *>(x->motor);
   B.features = static_cast<R *>(x->features);
   B.terms = static_cast<R *>(x->terms);
+  B.servoSupply = static_cast<R *>(x->servo_supply);
   B.contact = reinterpret_cast<bool *>(x->contact);
   B.histInit = reinterpret_cast<bool *>(x->history_initialized);
   B.done = reinterpret_cast<bool *>(x->done);
@@ -840,6 +850,17 @@ enum BamPart { kBamBegin = 1, kBamSubstep = 2, kBamFinish = 4, kBamServoOnly = 8
 template <class R>
 void bamRun(duck_batch *b, const BamKernelParams &k, const duck_bam_buffers *x, const void *actions, int parts,
             int substeps, cudaStream_t s) {
+  static_assert(kMaxBodies * 18 * 32 * sizeof(double) <= 160 * 1024, "RNEA shared arrays");
+  // Raise the loads kernel's shared-memory limit when a model needs more than
+  // any before (the first, eager step does it, so captures never need to).
+  static int rneaLimit[2][64] = {};
+  const int need = int(18 * b->nb * 32 * sizeof(R));
+  int &limit = rneaLimit[sizeof(R) == 8][b->device & 63];
+  if (need > limit) {
+    check(cudaFuncSetAttribute(bamLoadsKernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, need),
+          "cudaFuncSetAttribute");
+    limit = need;
+  }
   BamBuffers<R> B = bamBuffers<R>(x);
   B.envMass = static_cast<const R *>(b->envMass);
   B.envInertia = static_cast<const R *>(b->envInertia);
@@ -850,17 +871,20 @@ void bamRun(duck_batch *b, const BamKernelParams &k, const duck_bam_buffers *x, 
     bamBeginKernel<R><<<grid, 128, 0, s>>>(k, B, b->n, static_cast<const R *>(actions));
     ++b->launches;
   }
-  if (parts & kBamServoOnly) {
-    bamServoKernel<R><<<grid, 128, 0, s>>>(m, rec, b->recordStride, b->n, k, B);
-    ++b->launches;
-  }
+  const size_t rneaBytes = size_t(18) * b->nb * 32 * sizeof(R);
+  auto servo = [&] {
+    bamLoadsKernel<R><<<blocksFor(b->n, 32), 32, rneaBytes, s>>>(m, rec, b->recordStride, b->n, k, B);
+    bamServoJointKernel<R><<<blocksFor(size_t(b->n) * b->nj, 128), 128, 0, s>>>(m, rec, b->recordStride, b->n, k, B);
+    b->launches += 2;
+  };
+  if (parts & kBamServoOnly) servo();
   if (parts & kBamSubstep) {
     for (int i = 0; i < substeps; ++i) {
-      bamServoKernel<R><<<grid, 128, 0, s>>>(m, rec, b->recordStride, b->n, k, B);
+      servo();
       StepArgs args{nullptr, x->zero_forces, x->motor, 1, 0.0, 0.0};
       launchAdvance<R>(b, args, s);
       bamAfterKernel<R><<<grid, 128, 0, s>>>(m, rec, b->recordStride, b->n, k, B);
-      b->launches += 2;
+      ++b->launches;
     }
   }
   if (parts & kBamFinish) {

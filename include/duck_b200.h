@@ -272,6 +272,7 @@ typedef struct duck_bam_buffers {
   int64_t *episode_length;                         /* [E] */
   int32_t *counters;                               /* [2]: delay-ring cursor, common step counter */
   float *obs_actor, *obs_critic, *reward;          /* [E,19+3J], [E,duck_bam_critic_dim], [E] */
+  void *servo_supply;                              /* [E] scratch: servo supply voltage */
 } duck_bam_buffers;
 
 /* Critic observation width (76 for 14 joints, +3 with the mean-velocity
