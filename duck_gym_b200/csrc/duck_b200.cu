@@ -145,6 +145,7 @@ template <class R> duck_batch *create(const ParsedModel &parsed, int n, double d
   b->recordStride = (b->recordLength + 31) & ~31;
   b->layout = makeLayout(hm->dev);
   b->T = teamSize(hm->dev.colorMax);
+  scheduleSweep(hm->dev, b->T);
   b->teamsPerBlock = 32 / b->T;
   b->smemPerBlock = int(b->teamsPerBlock * b->layout.size * sizeof(R));
   int maxShared = 0;

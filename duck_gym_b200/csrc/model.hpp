@@ -30,6 +30,15 @@ template <class R> struct DevModel {
   int bound;         // contact bound of the portable record: pairs + 4 per ground shape
   int groundCap;     // on-chip ground contact capacity: sum of min(4, points) per ground shape
   int colorMax;      // largest number of dynamic bodies sharing one hinge colour
+  // Sweep schedule of the two model colours for the batch's team width, set
+  // by scheduleSweep (1 lane per body only): lane l of colour c handles body
+  // sweep[c][l][0] (-1: idle) and its hinges csrJoint[sweep[c][l][1] ..
+  // sweep[c][l][2]).  sweep[c][l][3] is -1 for a lane that owns its body
+  // alone, the helper's lane for an owner with a helper, and 32 + the owner's
+  // lane for a helper, which stamps only its hinges and hands its partial H
+  // and g to the owner.  sweepHelpers[c] = 1 when colour c has a helper.
+  int sweepScheduled, sweepHelpers[2];
+  alignas(16) int sweep[2][32][4];
   int ground, iterations;
   R dt, alpha, gamma, betaLinear, betaAngular, tolerance;
   R gravity[3];
@@ -59,6 +68,61 @@ template <class R> struct DevModel {
   int pA[kMaxPairs], pB[kMaxPairs];
   R pFriction[kMaxPairs];
 };
+
+// Lanes of a team sweep one colour at a time, one body per lane, and a warp
+// runs as long as its busiest lane: the body with the most hinges sets the
+// pace.  Where a colour has fewer bodies than the team has lanes, the spare
+// lanes help the bodies with the most hinges, taking the second half of
+// their hinge list, as long as that lowers the colour's largest hinge count.
+// Only models whose colours never change (no body-collision pairs) and teams
+// of one lane per body (T <= 8) are scheduled.
+template <class R> void scheduleSweep(DevModel<R> &d, int T) {
+  d.sweepScheduled = 0;
+  d.sweepHelpers[0] = d.sweepHelpers[1] = 0;
+  if (d.np != 0 || T > 8) return;
+  for (int c = 0; c < 2; ++c)
+    if (d.colorStart[c + 1] - d.colorStart[c] > T) return;
+  for (int c = 0; c < 2; ++c) {
+    int owner[32], begin[32], end[32], role[32];
+    const int n = d.colorStart[c + 1] - d.colorStart[c];
+    for (int l = 0; l < 32; ++l) { owner[l] = -1; begin[l] = end[l] = 0; role[l] = -1; }
+    for (int l = 0; l < n; ++l) {
+      const int b = d.colorBody[d.colorStart[c] + l];
+      owner[l] = b;
+      begin[l] = d.csrOffset[b];
+      end[l] = d.csrOffset[b + 1];
+    }
+    int spare = T - n, next = n;
+    for (;;) {
+      int most = 0, count = 0;
+      for (int l = 0; l < next; ++l) most = std::max(most, end[l] - begin[l]);
+      for (int l = 0; l < next; ++l) count += end[l] - begin[l] == most;
+      if (most < 2 || count > spare) break;
+      for (int l = 0, hi = next; l < hi; ++l) {
+        if (end[l] - begin[l] != most || role[l] >= 32) continue;
+        if (role[l] >= 0) { spare = 0; break; }   // one helper per owner
+        const int h = next++;
+        const int keep = (most + 1) / 2;
+        owner[h] = owner[l];
+        begin[h] = begin[l] + keep;
+        end[h] = end[l];
+        end[l] = begin[l] + keep;
+        role[l] = h;
+        role[h] = 32 + l;
+        --spare;
+        d.sweepHelpers[c] = 1;
+      }
+      if (spare <= 0) break;
+    }
+    for (int l = 0; l < 32; ++l) {
+      d.sweep[c][l][0] = owner[l];
+      d.sweep[c][l][1] = begin[l];
+      d.sweep[c][l][2] = end[l];
+      d.sweep[c][l][3] = role[l];
+    }
+  }
+  d.sweepScheduled = 1;
+}
 
 struct DVec { double x = 0, y = 0, z = 0; };
 struct DQuat { double w = 1, x = 0, y = 0, z = 0; };

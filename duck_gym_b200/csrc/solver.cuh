@@ -807,18 +807,21 @@ template <class R, int T> struct Solver {
     }
   }
 
-  // Block update of body bi (kernel.cuh:828-936).
+  // Block update of body bi (kernel.cuh:828-936), in two halves:
+  // assembleBody forms H and g, applyBody solves and moves the body.
   // With kSplit = 2 the two lanes of a pair (part 0 and 1) take alternate
   // items -- the inertia block, then each hinge, then each contact -- and
   // add their partial H and g with one shuffle per entry; both then solve
   // the same system and part 0 writes the pose.
-  __device__ __forceinline__ R updateBody(int bi, R kp, R limit, int part = 0) {
-    const R h = m->dt, alpha = m->alpha;
+  // The hinges taken are csrJoint[adjBegin, adjEnd); whole = false (a helper
+  // lane of the sweep schedule) leaves out the inertia block and contacts.
+  __device__ __forceinline__ void assembleBody(int bi, int adjBegin, int adjEnd, bool whole, R kp, R limit, int part,
+                                               R (&H)[21], R (&g)[6]) const {
+    const R h = m->dt;
     int item = 0;
     auto mine = [&]() { return kSplit == 1 || (item++ & 1) == part; };
     const R ih = R(1) / h, ih2 = ih * ih;
     const R mass = massOf(bi);
-    R H[21], g[6];
 #pragma unroll
     for (int i = 0; i < 21; ++i) H[i] = R(0);
 #pragma unroll
@@ -826,7 +829,7 @@ template <class R, int T> struct Solver {
     const V3<R> x = ld3(L.X + 3 * bi), xp = ld3(L.XQP + 7 * bi);
     const Q4<R> q = quat(bi), qp = ld4(L.XQP + 7 * bi + 3);
     // Inertia block with the SO(3) log Jacobian and frozen world inertia.
-    if (mine()) {
+    if (whole && mine()) {
       V3<R> dx = x - xp, th = fqlog(qmul(q, conj(qp)));
       R ml = mass * ih2;
       H[tri(0, 0)] = ml; H[tri(1, 1)] = ml; H[tri(2, 2)] = ml;
@@ -866,7 +869,6 @@ template <class R, int T> struct Solver {
     // Hinges touching bi, in CSR order.  One inlined copy of the hinge rows:
     // the Gauss-Seidel loop is instruction-fetch bound, so its code is kept
     // small rather than unrolled over hinge pairs.
-    const int adjBegin = ldg(m->csrOffset[bi]), adjEnd = ldg(m->csrOffset[bi + 1]);
     for (int adj = adjBegin; adj < adjEnd; ++adj) {
       if (!mine()) continue;
       const int j = ldg(m->csrJoint[adj]);
@@ -881,9 +883,10 @@ template <class R, int T> struct Solver {
     // touch bi, in list order: from the per-body bit mask when the list fits
     // 64 entries, else by scanning the list.
     const bool useMask = L.cap <= 64;
-    unsigned long long mask =
-        useMask ? unsigned(I[L.masks + 2 * bi]) | (unsigned long long)unsigned(I[L.masks + 2 * bi + 1]) << 32 : 0ull;
-    const int count = useMask ? 0 : I[iCount];
+    unsigned long long mask = useMask && whole ? unsigned(I[L.masks + 2 * bi]) |
+                                                     (unsigned long long)unsigned(I[L.masks + 2 * bi + 1]) << 32
+                                               : 0ull;
+    const int count = useMask || !whole ? 0 : I[iCount];
     int scan = 0;
     for (;;) {
       int ci = -1;
@@ -909,6 +912,13 @@ template <class R, int T> struct Solver {
 #pragma unroll
       for (int i = 0; i < 6; ++i) g[i] += __shfl_xor_sync(pair, g[i], 1);
     }
+  }
+
+  // Solve H st = -g, clamp the step (0.1 m, 0.25 rad) and move body bi;
+  // returns the applied step length (kernel.cuh:928-936).
+  __device__ __forceinline__ R applyBody(int bi, const R (&H)[21], const R (&g)[6], int part) {
+    const V3<R> x = ld3(L.X + 3 * bi);
+    const Q4<R> q = quat(bi);
     R st[6];
     if (!solve(H, g, st)) {
 #pragma unroll
@@ -1009,18 +1019,18 @@ template <class R, int T> struct Solver {
     }
     team.sync();
     // Predictor (kernel.cuh:965-976), one lane per body.  The predicted pose
-    // takes over the velocity slots of the body; x0 and q0 stay in registers
-    // until velocity recovery, which uses the same lane for the same body.
-    V3<R> x0r[kPerLane];
-    Q4<R> q0r[kPerLane];
+    // takes over the velocity slots of the body.  x0 and q0 wait for velocity
+    // recovery (the same lane, the same body) in the body's pose slots of the
+    // record, which nothing reads before store() rewrites them at the end of
+    // the call: held in registers they would stay live through every sweep.
 #pragma unroll
     for (int k = 0; k < kPerLane; ++k) {
       const int b = team.lane + k * T;
       if (b >= nb) continue;
       const V3<R> x = ld3(L.X + 3 * b);
       const Q4<R> q = quat(b);
-      x0r[k] = x;
-      q0r[k] = q;
+      R *r0 = rec + kRecHeader + kRecBody * b;
+      r0[0] = x.x; r0[1] = x.y; r0[2] = x.z; r0[3] = q.w; r0[4] = q.x; r0[5] = q.y; r0[6] = q.z;
       const R mass = massOf(b);
       if (mass == R(0)) continue;
       V3<R> in = inertiaOf(b);
@@ -1052,7 +1062,8 @@ template <class R, int T> struct Solver {
     team.sync();
     const int colorCount = m->np > 0 ? I[iColors] : 2;
     const R tol = m->tolerance;
-    for (int it = 0; it < m->iterations; ++it) {
+    const int iterations = m->iterations;
+    for (int it = 0; it < iterations; ++it) {
       R maxUpdate = R(0);
       for (int color = 0; color < colorCount; ++color) {
         int begin, end;
@@ -1063,10 +1074,42 @@ template <class R, int T> struct Solver {
           begin = ldg(m->colorStart[color]);
           end = ldg(m->colorStart[color + 1]);
         }
-        for (int slot = begin + team.lane / kSplit; slot < end; slot += T / kSplit) {
-          const int bi = m->np > 0 ? I[L.colorList + slot] : ldg(m->colorBody[slot]);
-          maxUpdate = rmax(maxUpdate, updateBody(bi, kp, limit, team.lane % kSplit));
-        }
+        // Scheduled colours (scheduleSweep) give each lane at most one role.
+        const bool scheduled = color < 2 && m->sweepScheduled;
+        int slot = begin + team.lane / kSplit;
+        do {
+          int bi = -1, adjBegin = 0, adjEnd = 0, role = -1;
+          if (scheduled) {
+            const int4 sc = __ldg(reinterpret_cast<const int4 *>(m->sweep[color][team.lane]));
+            bi = sc.x;
+            adjBegin = sc.y;
+            adjEnd = sc.z;
+            role = sc.w;
+          } else if (slot < end) {
+            bi = m->np > 0 ? I[L.colorList + slot] : ldg(m->colorBody[slot]);
+            adjBegin = ldg(m->csrOffset[bi]);
+            adjEnd = ldg(m->csrOffset[bi + 1]);
+          }
+          const bool have = bi >= 0, owner = role < 32;
+          R H[21], g[6];
+          if (have) assembleBody(bi, adjBegin, adjEnd, owner, kp, limit, team.lane % kSplit, H, g);
+          if (scheduled && m->sweepHelpers[color]) {
+            // An owner adds its helper's partial H and g (team-wide shuffles).
+            const int src = role >= 0 && role < 32 ? role : team.lane;
+#pragma unroll
+            for (int i = 0; i < 21; ++i) {
+              const R v = __shfl_sync(team.mask, H[i], src, T);
+              if (src != team.lane) H[i] += v;
+            }
+#pragma unroll
+            for (int i = 0; i < 6; ++i) {
+              const R v = __shfl_sync(team.mask, g[i], src, T);
+              if (src != team.lane) g[i] += v;
+            }
+          }
+          if (have && owner) maxUpdate = rmax(maxUpdate, applyBody(bi, H, g, team.lane % kSplit));
+          slot += T / kSplit;
+        } while (!scheduled && slot < end);
         team.sync();
       }
       maxUpdate = team.max(maxUpdate);
@@ -1113,8 +1156,11 @@ template <class R, int T> struct Solver {
       const int b = team.lane + k * T;
       if (b >= nb || !(ldg(m->mass[b]) > R(0))) continue;
       V3<R> x = ld3(L.X + 3 * b);
-      V3<R> v = (x - x0r[k]) * (R(1) / h);
-      V3<R> w = fqlog(qmul(quat(b), conj(q0r[k]))) * (R(1) / h);
+      const R *r0 = rec + kRecHeader + kRecBody * b;
+      const V3<R> x0{r0[0], r0[1], r0[2]};
+      const Q4<R> q0{r0[3], r0[4], r0[5], r0[6]};
+      V3<R> v = (x - x0) * (R(1) / h);
+      V3<R> w = fqlog(qmul(quat(b), conj(q0))) * (R(1) / h);
       SV vw = S + (L.XQP + 7 * b);
       vw[0] = v.x; vw[1] = v.y; vw[2] = v.z; vw[3] = w.x; vw[4] = w.y; vw[5] = w.z;
       if (!isfinite(dot(x, x) + dot(v, v) + dot(w, w))) bad = true;
