@@ -982,6 +982,14 @@ template <class R, int T> struct Solver {
     return C;
   }
 
+  // Start-of-substep hinge values, angle and axis rate (kernel.cuh:951-964).
+  __device__ __forceinline__ void setJointStart(int j, const JointGeo &e) {
+#pragma unroll
+    for (int k = 0; k < 7; ++k) S[L.JC0 + 7 * j + k] = e.C[k];
+    S[L.JA0 + j] = e.angle;
+    S[L.JV0 + j] = dot(omega(e.b) - omega(e.a), e.axis);
+  }
+
   // ------------------------------------------------------------ substep
   struct Diag {
     R jointError, axisError, penetration;
@@ -989,7 +997,10 @@ template <class R, int T> struct Solver {
     bool converged;
   };
 
-  __device__ __forceinline__ bool step(Diag &diag, R kp, R limit) {
+  // cached: the previous substep of this call ended with the diagnostics
+  // pass, which left this substep's hinge values, angles and axis rates in
+  // JC0, JA0 and JV0 (the poses and velocities have not moved since).
+  __device__ __forceinline__ bool step(Diag &diag, R kp, R limit, bool cached) {
     const R h = m->dt, alpha = m->alpha, gamma = m->gamma;
     diag = {R(0), R(0), R(0), 0, 0, false};
     detectContacts();
@@ -1002,14 +1013,13 @@ template <class R, int T> struct Solver {
     const R ag = alpha * gamma;
     // Joint warm start (kernel.cuh:951-964), one lane per joint.
     for (int j = team.lane; j < nj; j += T) {
-      JointGeo e;
-      evalJoint(j, e);
-#pragma unroll
-      for (int k = 0; k < 7; ++k) S[L.JC0 + 7 * j + k] = e.C[k];
-      S[L.JA0 + j] = e.angle;
+      if (!cached) {
+        JointGeo e;
+        evalJoint(j, e);
+        setJointStart(j, e);
+      }
       S[L.JLF + j] *= ag;
       S[L.JPF + j] = rclamp(S[L.JPF + j] * gamma, R(1), R(1e7));
-      S[L.JV0 + j] = dot(omega(e.b) - omega(e.a), e.axis);
 #pragma unroll
       for (int k = 0; k < 7; ++k) {
         S[L.JL + 7 * j + k] *= ag;
@@ -1176,6 +1186,7 @@ template <class R, int T> struct Solver {
     for (int j = team.lane; j < nj; j += T) {
       JointGeo e;
       evalJoint(j, e);
+      setJointStart(j, e);   // the next substep's start values
       je = rmax(je, rmax(R(fabs(e.C[0])), rmax(R(fabs(e.C[1])), R(fabs(e.C[2])))));
       ae = rmax(ae, rmax(R(fabs(e.C[3])), R(fabs(e.C[4]))));
     }
@@ -1204,7 +1215,7 @@ template <class R, int T> struct Solver {
     }
     for (int k = 0; k < substeps; ++k) {
       Diag d;
-      bool ok = step(d, kp, limit);
+      bool ok = step(d, kp, limit, k > 0);
       team.sync();
       if (!ok || I[iFailed]) break;
       summary.jointError = rmax(summary.jointError, d.jointError);
