@@ -582,17 +582,39 @@ template <class R, int T> struct Solver {
   // ------------------------------------------------------------ 6x6 algebra
   // Packed lower triangle: (i, j), j <= i, at i (i + 1) / 2 + j.
   static __device__ __forceinline__ int tri(int i, int j) { return i * (i + 1) / 2 + j; }
-  // Row J = (e_k, r x e_k) with force f and stiffness p (kernel.cuh:164-176).
-  static __device__ __forceinline__ void stampLinear(R *H, R *g, int k, V3<R> r, R f, R p) {
-    V3<R> c = k == 0 ? V3<R>{R(0), r.z, -r.y} : (k == 1 ? V3<R>{-r.z, R(0), r.x} : V3<R>{r.y, -r.x, R(0)});
-    g[k] += f;
-    g[3] += c.x * f; g[4] += c.y * f; g[5] += c.z * f;
-    H[tri(k, k)] += p;
-    H[tri(3, k)] += p * c.x; H[tri(4, k)] += p * c.y; H[tri(5, k)] += p * c.z;
-    V3<R> pc = c * p;
-    H[tri(3, 3)] += pc.x * c.x;
-    H[tri(4, 3)] += pc.y * c.x; H[tri(4, 4)] += pc.y * c.y;
-    H[tri(5, 3)] += pc.z * c.x; H[tri(5, 4)] += pc.z * c.y; H[tri(5, 5)] += pc.z * c.z;
+  // The three unit-axis rows J_k = (e_k, r x e_k), k = x, y, z, with forces
+  // f_k and stiffnesses p_k (hinge anchor rows, ground contacts): the
+  // reference's three rank-one stamps (kernel.cuh:164-176) in their order,
+  // entry by entry, leaving out the products with a structural zero of
+  // r x e_k.
+  static __device__ __forceinline__ void stampAxes(R *H, R *g, V3<R> r, R f0, R f1, R f2, R p0, R p1, R p2) {
+    // k = x: r x e_x = (0, z, -y).
+    g[0] += f0;
+    g[4] += r.z * f0; g[5] -= r.y * f0;
+    H[tri(0, 0)] += p0;
+    H[tri(4, 0)] += p0 * r.z; H[tri(5, 0)] -= p0 * r.y;
+    {
+      const R py = r.z * p0, pz = r.y * p0;
+      H[tri(4, 4)] += py * r.z; H[tri(5, 4)] -= pz * r.z; H[tri(5, 5)] += pz * r.y;
+    }
+    // k = y: r x e_y = (-z, 0, x).
+    g[1] += f1;
+    g[3] -= r.z * f1; g[5] += r.x * f1;
+    H[tri(1, 1)] += p1;
+    H[tri(3, 1)] -= p1 * r.z; H[tri(5, 1)] += p1 * r.x;
+    {
+      const R px = r.z * p1, pz = r.x * p1;
+      H[tri(3, 3)] += px * r.z; H[tri(5, 3)] -= pz * r.z; H[tri(5, 5)] += pz * r.x;
+    }
+    // k = z: r x e_z = (y, -x, 0).
+    g[2] += f2;
+    g[3] += r.y * f2; g[4] -= r.x * f2;
+    H[tri(2, 2)] += p2;
+    H[tri(3, 2)] += p2 * r.y; H[tri(4, 2)] -= p2 * r.x;
+    {
+      const R px = r.y * p2, py = r.x * p2;
+      H[tri(3, 3)] += px * r.y; H[tri(4, 3)] -= py * r.y; H[tri(4, 4)] += py * r.x;
+    }
   }
   // Row J = (0, c).
   static __device__ __forceinline__ void stampAngular(R *H, R *g, V3<R> c, R f, R p) {
@@ -716,10 +738,9 @@ template <class R, int T> struct Solver {
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
       R c = e.C[k] - alpha * c0[k];
-      R f = lam[k] + pen[k] * c;
-      f3[k] = f;
-      stampLinear(H, g, k, r, s * f, pen[k]);
+      f3[k] = lam[k] + pen[k] * c;
     }
+    stampAxes(H, g, r, s * f3[0], s * f3[1], s * f3[2], pen[0], pen[1], pen[2]);
     // Anchor rows: lever (parent ? ra : -rb) under unit-axis forces f_k e_k;
     // the majorizer depends on the lever only through its squares.
     geometricAxes(H, r, f3[0], f3[1], f3[2]);
@@ -781,9 +802,7 @@ template <class R, int T> struct Solver {
       C.z -= alpha * c[cC0];
       V3<R> f = coneForce(C, c);
       if (f.z < R(0)) {
-        stampLinear(H, g, 0, ra, f.x, c[cPenalty]);
-        stampLinear(H, g, 1, ra, f.y, c[cPenalty + 1]);
-        stampLinear(H, g, 2, ra, f.z, c[cPenalty + 2]);
+        stampAxes(H, g, ra, f.x, f.y, f.z, c[cPenalty], c[cPenalty + 1], c[cPenalty + 2]);
         geometric(H, ra, f);
       }
     } else {
