@@ -24,6 +24,7 @@ This module restates rsl-rl's published PPO algorithm in plain torch:
 from __future__ import annotations
 
 import math
+import warnings
 from dataclasses import dataclass
 
 import torch
@@ -49,6 +50,8 @@ class PPOConfig:
     critic_hidden: tuple = (512, 256, 128)
     bf16: bool = True
     bucket_mb: float = 0.5
+    graph_rollout: bool = True   # replay the rollout's policy step from a CUDA graph (GPU only)
+    graph_update: bool = True    # replay the update's minibatch step from CUDA graphs (GPU only)
 
 
 def mlp(sizes):
@@ -69,7 +72,9 @@ class ActorCritic(nn.Module):
         self.bf16 = cfg.bf16
 
     def _autocast(self, x):
-        return torch.autocast(x.device.type, dtype=torch.bfloat16, enabled=self.bf16)
+        # No cast cache: each region casts every weight once anyway, and a
+        # cache is not allowed inside a captured CUDA graph.
+        return torch.autocast(x.device.type, dtype=torch.bfloat16, enabled=self.bf16, cache_enabled=False)
 
     def mean(self, obs):
         with self._autocast(obs):
@@ -80,7 +85,9 @@ class ActorCritic(nn.Module):
             return self.critic(obs).float().squeeze(-1)
 
     def distribution(self, obs):
-        return torch.distributions.Normal(self.mean(obs), self.std.expand(obs.shape[0], -1))
+        # No argument validation (as rsl-rl's actor-critic sets): its checks
+        # read the tensors back on the host, which a CUDA graph cannot hold.
+        return torch.distributions.Normal(self.mean(obs), self.std.expand(obs.shape[0], -1), validate_args=False)
 
 
 class Storage:
@@ -142,6 +149,7 @@ class GradientAllReduce:
         self.world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
         self.params = [p for p in params if p.requires_grad]
         self.buckets, self.handles, self.pending = [], [], {}
+        self.enabled = True   # off once a captured update averages the gradients itself
         if self.world == 1:
             return
         limit = max(1, int(bucket_mb * 1e6 / 4))
@@ -162,6 +170,8 @@ class GradientAllReduce:
                 p.register_post_accumulate_grad_hook(self._ready)
 
     def _ready(self, p):
+        if not self.enabled:
+            return
         i = self.owner[p]
         self.pending[i] = self.pending.get(i, 0) + 1
         if self.pending[i] == len(self.buckets[i]):
@@ -174,7 +184,7 @@ class GradientAllReduce:
 
     def finish(self):
         """Wait for the bucket all-reduces and write the averages back."""
-        if self.world == 1:
+        if self.world == 1 or not self.enabled:
             return
         if len(self.handles) != len(self.buckets):
             raise RuntimeError("a gradient bucket was not reduced (unused parameters?)")
@@ -187,6 +197,27 @@ class GradientAllReduce:
                 q.grad.copy_(flat[offset:offset + n].view_as(q.grad))
                 offset += n
         self.handles, self.pending = [], {}
+
+
+def kl_schedule_host(lr: float, kl: float, desired: float) -> float:
+    """rsl-rl's adaptive learning rate (rsl_rl/algorithms/ppo.py, the
+    "adaptive" schedule): divide by 1.5 (not below 1e-5) when the KL exceeds
+    twice the desired value, multiply by 1.5 (not above 1e-2) when it is
+    positive and below half of it."""
+    if kl > 2.0 * desired:
+        return max(1e-5, lr / 1.5)
+    if 0.0 < kl < desired / 2.0:
+        return min(1e-2, lr * 1.5)
+    return lr
+
+
+def kl_schedule(lr: torch.Tensor, kl: torch.Tensor, desired: float) -> torch.Tensor:
+    """kl_schedule_host on device tensors (float64 learning rate; the KL is
+    compared in float64 like the host rule's Python floats)."""
+    kl = kl.double()
+    down = torch.clamp(lr / 1.5, min=1e-5)
+    up = torch.clamp(lr * 1.5, max=1e-2)
+    return torch.where(kl > 2.0 * desired, down, torch.where((kl > 0.0) & (kl < desired / 2.0), up, lr))
 
 
 class PPO:
@@ -208,8 +239,19 @@ class PPO:
             for p in self.policy.parameters():   # every rank starts from rank 0's weights
                 dist.broadcast(p.data, 0)
         self.reducer = GradientAllReduce(self.policy.parameters(), self.cfg.bucket_mb)
-        self.optimizer = torch.optim.Adam(self.policy.parameters(), lr=self.cfg.learning_rate)
-        self.learning_rate = self.cfg.learning_rate
+        # On the GPU the learning rate lives on the device (fused Adam reads it
+        # there) and the KL schedule updates it there, so an update never
+        # waits for the host; on the CPU it is a Python float.
+        if self.device.type == "cuda":
+            self._lr64 = torch.tensor(self.cfg.learning_rate, dtype=torch.float64, device=self.device)
+            self._lr = self._lr64.float()
+            self.optimizer = torch.optim.Adam(self.policy.parameters(), lr=self._lr, fused=True, capturable=True)
+        else:
+            self._lr64 = self._lr = None
+            self.optimizer = torch.optim.Adam(self.policy.parameters(), lr=self.cfg.learning_rate)
+            self._host_lr = self.cfg.learning_rate
+        self._graph = None
+        self._updates, self._ugraphs = 0, None
         self.storage = Storage(self.cfg.steps_per_env, env.num_envs, self.obs.shape[1], self.critic_obs.shape[1],
                                env.num_actions, self.device)
 
@@ -219,18 +261,49 @@ class PPO:
             return obs["actor"].to(self.device), obs["critic"].to(self.device)
         return obs.to(self.device), obs.to(self.device)
 
+    def _act(self, obs, critic_obs):
+        """One rollout step of the policy: sampled actions, their summed log
+        probability, the distribution's mean and std, and the value."""
+        d = self.policy.distribution(obs)
+        # mean + std * N(0, 1) drawn in place: the same draw as sample(), whose
+        # torch.normal(mean, std) checks std >= 0 on the host (no graph).
+        actions = d.rsample()
+        return actions, d.log_prob(actions).sum(-1), d.mean, d.stddev, self.policy.value(critic_obs)
+
+    def _act_graphed(self, obs, critic_obs):
+        """_act replayed from a CUDA graph: the policy's 30-odd small kernels
+        are one launch, so a rollout step no longer waits on the host.  The
+        graph reads the parameters in place, so it stays valid across
+        optimizer steps; the samples come from the default CUDA generator."""
+        if self._graph is None:
+            self._graph_in = (obs.clone(), critic_obs.clone())
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    self._act(*self._graph_in)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self._graph_out = self._act(*self._graph_in)
+            self._graph = graph
+        self._graph_in[0].copy_(obs)
+        self._graph_in[1].copy_(critic_obs)
+        self._graph.replay()
+        return self._graph_out
+
     @torch.no_grad()
     def rollout(self):
         s, cfg = self.storage, self.cfg
+        act = self._act_graphed if self.device.type == "cuda" and cfg.graph_rollout else self._act
         for t in range(cfg.steps_per_env):
-            d = self.policy.distribution(self.obs)
-            actions = d.sample()
+            actions, log_prob, mu, sigma, values = act(self.obs, self.critic_obs)
             s.obs[t], s.critic_obs[t] = self.obs, self.critic_obs
             s.actions[t] = actions
-            s.log_prob[t] = d.log_prob(actions).sum(-1)
-            s.mu[t], s.sigma[t] = d.mean, d.stddev
-            s.values[t] = self.policy.value(self.critic_obs)
-            obs, reward, done, info = self.env.step(actions)
+            s.log_prob[t] = log_prob
+            s.mu[t], s.sigma[t] = mu, sigma
+            s.values[t] = values
+            obs, reward, done, info = self.env.step(s.actions[t])
             reward = reward.to(self.device).float()
             if "time_outs" in info:
                 reward = reward + cfg.gamma * s.values[t] * info["time_outs"].to(self.device).float()
@@ -238,11 +311,20 @@ class PPO:
             s.dones[t] = done.to(self.device).float()
             self.obs, self.critic_obs = self._split(obs)
         last = self.policy.value(self.critic_obs)
-        s.returns, s.advantages = gae(s.rewards, s.dones, s.values, last, cfg.gamma, cfg.lam)
-        a = s.advantages
-        s.advantages = (a - a.mean()) / (a.std() + 1e-8)
+        returns, advantages = gae(s.rewards, s.dones, s.values, last, cfg.gamma, cfg.lam)
+        s.returns.copy_(returns)   # in place: a captured update reads these buffers
+        s.advantages.copy_((advantages - advantages.mean()) / (advantages.std() + 1e-8))
+
+    STATS = ("surrogate", "value", "entropy", "kl")
 
     def update(self, generator=None):
+        """epochs x mini_batches PPO steps over the last rollout.  On the GPU
+        every update after the first (which also creates the optimizer state)
+        replays CUDA graphs of the minibatch step, so no step waits on the
+        host; the minibatch order is drawn eagerly, as before."""
+        if self.device.type == "cuda" and self.cfg.graph_update and self._updates > 0:
+            return self._update_graphed(generator)
+        self._updates += 1
         s, cfg = self.storage, self.cfg
         n = s.T * s.E
         flat = lambda x: x.reshape(n, *x.shape[2:])
@@ -260,9 +342,85 @@ class PPO:
                 loss.backward()
                 self.reducer.finish()
                 nn.utils.clip_grad_norm_(self.policy.parameters(), cfg.max_grad_norm)
-                self.optimizer.step()
+                with warnings.catch_warnings():   # capturable Adam stepped outside a graph
+                    warnings.simplefilter("ignore", UserWarning)
+                    self.optimizer.step()
                 stats.append(info)
         return {k: torch.stack([x[k] for x in stats]).mean().item() for k in stats[0]}
+
+    def _step_loss(self):
+        """Forward and backward of one minibatch (the rows self._idx of the
+        rollout), the KL in the last slot of the flat gradient buffer."""
+        data = [x.index_select(0, self._idx) for x in self._data]
+        loss, info = ppo_loss(self.policy, *data, self.cfg)
+        self.optimizer.zero_grad(set_to_none=False)
+        loss.backward()
+        self._flat_grad[-1:].copy_(info["kl"].reshape(1))
+        self._stats.copy_(torch.stack([info[k] for k in self.STATS]))
+
+    def _step_apply(self):
+        """KL learning-rate schedule, gradient clipping and the Adam step."""
+        if self.cfg.desired_kl is not None:
+            self._lr64.copy_(kl_schedule(self._lr64, self._flat_grad[-1], self.cfg.desired_kl))
+            self._lr.copy_(self._lr64)
+        nn.utils.clip_grad_norm_(self.policy.parameters(), self.cfg.max_grad_norm)
+        self.optimizer.step()
+
+    def _capture_update(self):
+        s, cfg = self.storage, self.cfg
+        n = s.T * s.E
+        self._data = [x.reshape(n, *x.shape[2:]) for x in (s.obs, s.critic_obs, s.actions, s.log_prob, s.mu,
+                                                             s.sigma, s.values, s.returns, s.advantages)]
+        self._idx = torch.zeros(n // cfg.mini_batches, dtype=torch.long, device=self.device)
+        self._stats = torch.zeros(len(self.STATS), device=self.device)
+        # The gradients become views of one flat buffer (plus a KL slot), so
+        # with several ranks one all-reduce between the two graphs averages
+        # the gradients and the KL together.
+        params = [p for p in self.policy.parameters() if p.requires_grad]
+        total = sum(p.numel() for p in params)
+        self._flat_grad = torch.zeros(total + 1, device=self.device)
+        offset = 0
+        for p in params:
+            view = self._flat_grad[offset:offset + p.numel()].view_as(p)
+            view.copy_(p.grad if p.grad is not None else torch.zeros_like(p))
+            p.grad = view
+            offset += p.numel()
+        self.reducer.enabled = False
+        graphs = []
+        parts = [[self._step_loss, self._step_apply]] if self.world == 1 else [[self._step_loss], [self._step_apply]]
+        for fns in parts:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for fn in fns:
+                    fn()
+            graphs.append(graph)
+        self._ugraphs = graphs
+
+    def _update_graphed(self, generator):
+        s, cfg = self.storage, self.cfg
+        if self._ugraphs is None:
+            self._capture_update()
+        n = s.T * s.E
+        size = n // cfg.mini_batches
+        stats = torch.empty(cfg.epochs * cfg.mini_batches, len(self.STATS), device=self.device)
+        k = 0
+        for _ in range(cfg.epochs):
+            order = torch.randperm(n, device=self.device, generator=generator)
+            for b in range(cfg.mini_batches):
+                self._idx.copy_(order[b * size:(b + 1) * size])
+                self._ugraphs[0].replay()
+                if self.world > 1:
+                    dist.all_reduce(self._flat_grad)
+                    self._flat_grad.div_(self.world)
+                    self._ugraphs[1].replay()
+                stats[k].copy_(self._stats)
+                k += 1
+        means = stats.mean(0).tolist()
+        return dict(zip(self.STATS, means))
+
+    @property
+    def learning_rate(self) -> float:
+        return float(self._lr64) if self._lr64 is not None else self._host_lr
 
     def _adapt(self, kl):
         """rsl-rl's adaptive schedule: lr / 1.5 above 2 x desired KL, x 1.5
@@ -273,13 +431,13 @@ class PPO:
             kl = kl.clone()
             dist.all_reduce(kl)
             kl /= self.world
-        kl = float(kl)
-        if kl > 2.0 * self.cfg.desired_kl:
-            self.learning_rate = max(1e-5, self.learning_rate / 1.5)
-        elif 0.0 < kl < self.cfg.desired_kl / 2.0:
-            self.learning_rate = min(1e-2, self.learning_rate * 1.5)
+        if self._lr64 is not None:
+            self._lr64.copy_(kl_schedule(self._lr64, kl, self.cfg.desired_kl))
+            self._lr.copy_(self._lr64)
+            return
+        self._host_lr = kl_schedule_host(self._host_lr, float(kl), self.cfg.desired_kl)
         for group in self.optimizer.param_groups:
-            group["lr"] = self.learning_rate
+            group["lr"] = self._host_lr
 
     def learn(self, iterations):
         history = []

@@ -30,3 +30,49 @@ def test_ppo_on_bam_env(tmp_path):
     s = agent.storage
     assert torch.isfinite(s.rewards).all() and s.dones.sum() > 0
     assert agent.obs.shape == (256, 61) and agent.critic_obs.shape[1] == 76
+
+
+def test_graphed_update_matches_eager(tmp_path):
+    """The update replayed from CUDA graphs takes the same steps as the eager
+    update: same minibatch order, same KL schedule, same clipped Adam steps
+    (parameters, optimizer state and learning rate restored in place between
+    the two runs)."""
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+    from duck_gym_b200 import biped
+    from duck_gym_b200.bam_env import BamEnv
+    from duck_gym_b200.ppo import PPO, PPOConfig
+
+    biped.write_bam(tmp_path, seed=0)
+    env = BamEnv(tmp_path, num_envs=256, iterations=10, auto_reset=True, reward_enabled=True, seconds=0.1)
+    agent = PPO(env, PPOConfig(steps_per_env=8), seed=0)
+    agent.rollout()
+    agent.update()          # eager: creates the optimizer state
+    agent.rollout()
+    params = [p for p in agent.policy.parameters()]
+    saved_params = [p.detach().clone() for p in params]
+    saved_state = [{k: v.clone() for k, v in agent.optimizer.state[p].items()} for p in params]
+    saved_lr = agent._lr64.clone()
+
+    def restore():
+        with torch.no_grad():
+            for p, v, st in zip(params, saved_params, saved_state):
+                p.copy_(v)
+                for k, t in st.items():
+                    agent.optimizer.state[p][k].copy_(t)
+            agent._lr64.copy_(saved_lr)
+            agent._lr.copy_(saved_lr)
+
+    agent.cfg.graph_update = False
+    eager_stats = agent.update(generator=torch.Generator(device="cuda").manual_seed(7))
+    eager = [p.detach().clone() for p in params]
+    eager_lr = agent.learning_rate
+    restore()
+    agent.cfg.graph_update = True
+    graphed_stats = agent.update(generator=torch.Generator(device="cuda").manual_seed(7))
+    assert agent._ugraphs is not None
+    for a, b in zip(eager, params):
+        torch.testing.assert_close(b.detach(), a, rtol=1e-5, atol=1e-6)
+    assert agent.learning_rate == pytest.approx(eager_lr, rel=1e-12)
+    for k in eager_stats:
+        assert graphed_stats[k] == pytest.approx(eager_stats[k], rel=1e-4, abs=1e-6)

@@ -134,3 +134,23 @@ def test_gradient_all_reduce_two_gloo_ranks():
             assert torch.equal(a0, a1)
         for p0, p1 in zip(out["params0"], out["params1"]):
             assert torch.equal(p0, p1)
+
+
+def test_device_kl_schedule_matches_host_rule():
+    """The learning-rate schedule run on device tensors (no host round trip)
+    follows the host rule step for step, including KLs at the thresholds,
+    zero, negative and NaN."""
+    import random
+
+    from duck_gym_b200.ppo import kl_schedule, kl_schedule_host
+
+    rng = random.Random(0)
+    host, dev = 3e-4, torch.tensor(3e-4, dtype=torch.float64)
+    for _ in range(3000):
+        kl = rng.choice([0.0, -1e-3, float("nan"), 0.02, 0.005, rng.uniform(0.0, 0.05), rng.uniform(0.004, 0.006),
+                         rng.uniform(0.019, 0.021)])
+        kl32 = torch.tensor(kl, dtype=torch.float32)
+        host = kl_schedule_host(host, float(kl32), 0.01)
+        dev = kl_schedule(dev, kl32, 0.01)
+        assert host == float(dev)
+    assert 1e-5 <= host <= 1e-2
