@@ -51,7 +51,7 @@ class PPOConfig:
     bf16: bool = True
     bucket_mb: float = 0.5
     graph_rollout: bool = True   # replay the rollout's policy step from a CUDA graph (GPU only)
-    graph_update: bool = True    # replay the update's minibatch step from CUDA graphs (GPU only)
+    graph_update: bool = True    # flat-gradient minibatch step after the first update, CUDA graphs on the GPU
 
 
 def mlp(sizes):
@@ -251,7 +251,7 @@ class PPO:
             self.optimizer = torch.optim.Adam(self.policy.parameters(), lr=self.cfg.learning_rate)
             self._host_lr = self.cfg.learning_rate
         self._graph = None
-        self._updates, self._ugraphs = 0, None
+        self._updates, self._ugraphs, self._flat_grad = 0, None, None
         self.storage = Storage(self.cfg.steps_per_env, env.num_envs, self.obs.shape[1], self.critic_obs.shape[1],
                                env.num_actions, self.device)
 
@@ -318,12 +318,13 @@ class PPO:
     STATS = ("surrogate", "value", "entropy", "kl")
 
     def update(self, generator=None):
-        """epochs x mini_batches PPO steps over the last rollout.  On the GPU
-        every update after the first (which also creates the optimizer state)
-        replays CUDA graphs of the minibatch step, so no step waits on the
-        host; the minibatch order is drawn eagerly, as before."""
-        if self.device.type == "cuda" and self.cfg.graph_update and self._updates > 0:
-            return self._update_graphed(generator)
+        """epochs x mini_batches PPO steps over the last rollout.  Every
+        update after the first (which also creates the optimizer state) runs
+        the minibatch step over a flat gradient buffer (_update_flat); on the
+        GPU that step is replayed from CUDA graphs, so no step waits on the
+        host.  The minibatch order is drawn eagerly either way."""
+        if self.cfg.graph_update and self._updates > 0:
+            return self._update_flat(generator)
         self._updates += 1
         s, cfg = self.storage, self.cfg
         n = s.T * s.E
@@ -360,13 +361,17 @@ class PPO:
 
     def _step_apply(self):
         """KL learning-rate schedule, gradient clipping and the Adam step."""
-        if self.cfg.desired_kl is not None:
+        if self.cfg.desired_kl is not None and self._lr64 is not None:
             self._lr64.copy_(kl_schedule(self._lr64, self._flat_grad[-1], self.cfg.desired_kl))
             self._lr.copy_(self._lr64)
+        elif self.cfg.desired_kl is not None:
+            self._host_lr = kl_schedule_host(self._host_lr, float(self._flat_grad[-1]), self.cfg.desired_kl)
+            for group in self.optimizer.param_groups:
+                group["lr"] = self._host_lr
         nn.utils.clip_grad_norm_(self.policy.parameters(), self.cfg.max_grad_norm)
         self.optimizer.step()
 
-    def _capture_update(self):
+    def _prepare_flat(self):
         s, cfg = self.storage, self.cfg
         n = s.T * s.E
         self._data = [x.reshape(n, *x.shape[2:]) for x in (s.obs, s.critic_obs, s.actions, s.log_prob, s.mu,
@@ -386,20 +391,30 @@ class PPO:
             p.grad = view
             offset += p.numel()
         self.reducer.enabled = False
-        graphs = []
-        parts = [[self._step_loss, self._step_apply]] if self.world == 1 else [[self._step_loss], [self._step_apply]]
-        for fns in parts:
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                for fn in fns:
-                    fn()
-            graphs.append(graph)
-        self._ugraphs = graphs
+        # One part per side of the gradient all-reduce.
+        self._parts = [[self._step_loss, self._step_apply]] if self.world == 1 else [[self._step_loss],
+                                                                                      [self._step_apply]]
+        if self.device.type == "cuda":
+            graphs = []
+            for fns in self._parts:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for fn in fns:
+                        fn()
+                graphs.append(graph)
+            self._ugraphs = graphs
 
-    def _update_graphed(self, generator):
+    def _run_part(self, i):
+        if self._ugraphs is not None:
+            self._ugraphs[i].replay()
+        else:
+            for fn in self._parts[i]:
+                fn()
+
+    def _update_flat(self, generator):
         s, cfg = self.storage, self.cfg
-        if self._ugraphs is None:
-            self._capture_update()
+        if self._flat_grad is None:
+            self._prepare_flat()
         n = s.T * s.E
         size = n // cfg.mini_batches
         stats = torch.empty(cfg.epochs * cfg.mini_batches, len(self.STATS), device=self.device)
@@ -408,11 +423,11 @@ class PPO:
             order = torch.randperm(n, device=self.device, generator=generator)
             for b in range(cfg.mini_batches):
                 self._idx.copy_(order[b * size:(b + 1) * size])
-                self._ugraphs[0].replay()
+                self._run_part(0)
                 if self.world > 1:
                     dist.all_reduce(self._flat_grad)
                     self._flat_grad.div_(self.world)
-                    self._ugraphs[1].replay()
+                    self._run_part(1)
                 stats[k].copy_(self._stats)
                 k += 1
         means = stats.mean(0).tolist()

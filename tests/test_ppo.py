@@ -112,12 +112,16 @@ def _rank(rank, world, port, out):
     local = [p.grad.clone() for p in net.parameters()]
     reducer.finish()
     out[rank] = ([p.grad.clone() for p in net.parameters()], local, len(reducer.buckets))
-    # Two PPO updates on a toy env per rank stay in sync across ranks.
+    # Three PPO updates on a toy env per rank stay in sync across ranks: the
+    # first averages gradients through the bucket hooks, the others through
+    # the flat gradient buffer (one all-reduce with the KL slot).
     env = ToyEnv(n=16, seed=rank)
     agent = ppo.PPO(env, ppo.PPOConfig(bf16=False, steps_per_env=4, actor_hidden=(16,), critic_hidden=(16,)),
                     device="cpu", seed=rank)
-    agent.learn(2)
+    agent.learn(3)
     out[f"params{rank}"] = [p.detach().clone() for p in agent.policy.parameters()]
+    out[f"flat{rank}"] = agent._flat_grad is not None and not agent.reducer.enabled
+    out[f"lr{rank}"] = agent.learning_rate
     dist.destroy_process_group()
 
 
@@ -134,6 +138,7 @@ def test_gradient_all_reduce_two_gloo_ranks():
             assert torch.equal(a0, a1)
         for p0, p1 in zip(out["params0"], out["params1"]):
             assert torch.equal(p0, p1)
+        assert out["flat0"] and out["flat1"] and out["lr0"] == out["lr1"]
 
 
 def test_device_kl_schedule_matches_host_rule():
@@ -154,3 +159,24 @@ def test_device_kl_schedule_matches_host_rule():
         dev = kl_schedule(dev, kl32, 0.01)
         assert host == float(dev)
     assert 1e-5 <= host <= 1e-2
+
+
+def test_flat_update_matches_eager():
+    """The flat-gradient minibatch step (the one the GPU replays from CUDA
+    graphs) takes the same steps as the eager update on the CPU."""
+    def run(flat):
+        cfg = ppo.PPOConfig(bf16=False, steps_per_env=8, actor_hidden=(32, 32), critic_hidden=(32,),
+                            learning_rate=3e-3, graph_update=flat)
+        agent = ppo.PPO(ToyEnv(n=32, seed=3), cfg, device="cpu", seed=0)
+        history = agent.learn(4)
+        return agent, history
+
+    flat, flat_history = run(True)
+    eager, eager_history = run(False)
+    assert flat._flat_grad is not None and eager._flat_grad is None
+    for a, b in zip(flat.policy.parameters(), eager.policy.parameters()):
+        torch.testing.assert_close(a.detach(), b.detach(), rtol=1e-5, atol=1e-6)
+    assert flat.learning_rate == pytest.approx(eager.learning_rate, rel=1e-12)
+    for h0, h1 in zip(flat_history, eager_history):
+        for k in h1:
+            assert h0[k] == pytest.approx(h1[k], rel=1e-4, abs=1e-6)
