@@ -186,23 +186,59 @@ __device__ __forceinline__ int detectPairsBody(int base, int prevCount) {
   const R ag = xmul(m->alpha, m->gamma);
   const R *prev = rec + kRecHeader + kRecBody * m->nb + kRecJoint * m->nj;
   const int nGround = base;
+  // Pass 1, one lane per pair: the bounding-sphere test with the velocity
+  // skin (kernel.cuh:656-664).  The pairs that pass are the narrow phase's
+  // candidates; they are listed in pair order in the free contact entries
+  // from nGround on (pair index in the meta word, skin in the c0 word), which
+  // the contacts written in pass 2 overtake only after they are read.
+  int candidates = 0;
   for (int first = 0; first < m->np; first += T) {
     const int pi = first + team.lane;
-    Hit hit{0, {R(0), R(0), R(0)}, {R(0), R(0), R(0)}, R(0)};
+    bool close = false;
     R skin = R(0);
-    int sa = 0, sb = 0, ba = 0, bb = 0;
     if (pi < m->np) {
-      sa = ldg(m->pA[pi]);
-      sb = ldg(m->pB[pi]);
-      ba = ldg(m->sBody[sa]);
-      bb = ldg(m->sBody[sb]);
+      const int sa = ldg(m->pA[pi]), sb = ldg(m->pB[pi]);
+      const int ba = ldg(m->sBody[sa]), bb = ldg(m->sBody[sb]);
       if (!(ldg(m->mass[ba]) == R(0) && ldg(m->mass[bb]) == R(0))) {
         const R radA = ldg(m->sRadius[sa]), radB = ldg(m->sRadius[sb]);
         skin = xadd(R(.003), xmul(dt, xadd(xadd(xnorm(xsub(vel(ba), vel(bb))), xmul(xnorm(omega(ba)), radA)),
                                              xmul(xnorm(omega(bb)), radB))));
-        if (!(xnorm(xsub(ld3(L.X + 3 * ba), ld3(L.X + 3 * bb))) > xadd(xadd(radA, radB), skin)))
-          hit = xconvexContact(sa, sb, skin, tolerance);
+        close = !(xnorm(xsub(ld3(L.X + 3 * ba), ld3(L.X + 3 * bb))) > xadd(xadd(radA, radB), skin));
       }
+    }
+    int total;
+    const int at = nGround + candidates + team.scan(close ? 1 : 0, &total);
+    if (close) {
+      if (at < L.cap) {
+        cmeta(at) = pi;
+        contact(at)[cC0] = skin;
+      } else {
+        I[iFailed] = 1;
+      }
+    }
+    candidates += total;
+  }
+  candidates = nGround + candidates <= L.cap ? candidates : L.cap - nGround;
+  team.sync();
+  // Pass 2: the narrow phase (MPR) over the candidates only, so a team's
+  // rounds of the costly portal search follow the number of close pairs, not
+  // where they sit in the pair list.  Hits keep pair order.
+  for (int first = 0; first < candidates; first += T) {
+    const int k = first + team.lane;
+    Hit hit{0, {R(0), R(0), R(0)}, {R(0), R(0), R(0)}, R(0)};
+    R skin = R(0);
+    int pi = 0, sa = 0, sb = 0, ba = 0, bb = 0;
+    if (k < candidates) {
+      pi = cmeta(nGround + k);
+      skin = contact(nGround + k)[cC0];
+    }
+    team.sync();   // every candidate of this round is read before contacts are written
+    if (k < candidates) {
+      sa = ldg(m->pA[pi]);
+      sb = ldg(m->pB[pi]);
+      ba = ldg(m->sBody[sa]);
+      bb = ldg(m->sBody[sb]);
+      hit = xconvexContact(sa, sb, skin, tolerance);
       if (hit.status < 0) I[iFailed] = 1;
     }
     const int found = hit.status == 1 ? 1 : 0;
