@@ -45,7 +45,7 @@ int teamSize(int colorMax) {
 }  // namespace
 
 struct duck_batch {
-  int device = 0, fp64 = 0, n = 0, nb = 0, nj = 0, bound = 0, recordLength = 0, recordStride = 0;
+  int device = 0, fp64 = 0, n = 0, nb = 0, nj = 0, np = 0, bound = 0, recordLength = 0, recordStride = 0;
   int T = 8, teamsPerBlock = 4, smemPerBlock = 0;
   Layout layout{};
   void *devModel = nullptr, *points = nullptr, *records = nullptr;
@@ -91,17 +91,23 @@ void finish(duck_batch *b, cudaStream_t s) {
 }
 int blocksFor(long long threads, int per) { return int((threads + per - 1) / per); }
 
+// The step kernel instantiation for a batch: its team width, and whether its
+// model has body-collision pairs (without them the pair code is compiled out).
+template <class R, class F> void withAdvance(const duck_batch *b, F &&f) {
+  const bool pairs = b->np > 0;
+  switch (b->T) {
+    case 4: pairs ? f(advanceKernel<R, 4, true>) : f(advanceKernel<R, 4, false>); break;
+    case 8: pairs ? f(advanceKernel<R, 8, true>) : f(advanceKernel<R, 8, false>); break;
+    case 16: pairs ? f(advanceKernel<R, 16, true>) : f(advanceKernel<R, 16, false>); break;
+    default: pairs ? f(advanceKernel<R, 32, true>) : f(advanceKernel<R, 32, false>); break;
+  }
+}
+
 template <class R> void setupAdvance(duck_batch *b) {
-  auto set = [&](auto kernel) {
+  withAdvance<R>(b, [&](auto kernel) {
     check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, b->smemPerBlock),
           "cudaFuncSetAttribute");
-  };
-  switch (b->T) {
-    case 4: set(advanceKernel<R, 4>); break;
-    case 8: set(advanceKernel<R, 8>); break;
-    case 16: set(advanceKernel<R, 16>); break;
-    default: set(advanceKernel<R, 32>); break;
-  }
+  });
 }
 
 template <class R> void launchAdvance(duck_batch *b, const StepArgs &stepArgs, cudaStream_t s) {
@@ -113,12 +119,9 @@ template <class R> void launchAdvance(duck_batch *b, const StepArgs &stepArgs, c
   const R *pts = static_cast<const R *>(b->points);
   const DevModel<R> *m = static_cast<const DevModel<R> *>(b->devModel);
   R *rec = static_cast<R *>(b->records);
-  switch (b->T) {
-    case 4: advanceKernel<R, 4><<<grid, 32, b->smemPerBlock, s>>>(m, pts, rec, b->recordStride, b->n, b->layout, args); break;
-    case 8: advanceKernel<R, 8><<<grid, 32, b->smemPerBlock, s>>>(m, pts, rec, b->recordStride, b->n, b->layout, args); break;
-    case 16: advanceKernel<R, 16><<<grid, 32, b->smemPerBlock, s>>>(m, pts, rec, b->recordStride, b->n, b->layout, args); break;
-    default: advanceKernel<R, 32><<<grid, 32, b->smemPerBlock, s>>>(m, pts, rec, b->recordStride, b->n, b->layout, args); break;
-  }
+  withAdvance<R>(b, [&](auto kernel) {
+    kernel<<<grid, 32, b->smemPerBlock, s>>>(m, pts, rec, b->recordStride, b->n, b->layout, args);
+  });
   ++b->launches;
 }
 
@@ -139,6 +142,7 @@ template <class R> duck_batch *create(const ParsedModel &parsed, int n, double d
   b->n = n;
   b->nb = hm->dev.nb;
   b->nj = hm->dev.nj;
+  b->np = hm->dev.np;
   b->bound = hm->dev.bound;
   b->names = hm->jointNames;
   b->recordLength = kRecHeader + kRecBody * b->nb + kRecJoint * b->nj + kRecContact * b->bound;
@@ -533,12 +537,7 @@ void referenceStatic(const duck_batch *b, char *scratch, size_t recordBytes, con
   const int stride = b->recordStride;
   check(cudaMemset(scratch, 0, recordBytes), "cudaMemset scratch record");
   resetKernel<R><<<1, 128>>>(m, rec, stride, 1, nullptr, nullptr, nullptr, 0);
-  switch (b->T) {
-    case 4: advanceKernel<R, 4><<<1, 32, b->smemPerBlock>>>(m, pts, rec, stride, 1, b->layout, args); break;
-    case 8: advanceKernel<R, 8><<<1, 32, b->smemPerBlock>>>(m, pts, rec, stride, 1, b->layout, args); break;
-    case 16: advanceKernel<R, 16><<<1, 32, b->smemPerBlock>>>(m, pts, rec, stride, 1, b->layout, args); break;
-    default: advanceKernel<R, 32><<<1, 32, b->smemPerBlock>>>(m, pts, rec, stride, 1, b->layout, args); break;
-  }
+  withAdvance<R>(b, [&](auto kernel) { kernel<<<1, 32, b->smemPerBlock>>>(m, pts, rec, stride, 1, b->layout, args); });
   snapshotKernel<R><<<1, 64>>>(m, rec, stride, 1, reinterpret_cast<R *>(dBodies), reinterpret_cast<R *>(dJoints),
                                reinterpret_cast<R *>(dDiag));
   check(cudaGetLastError(), "static reference launch");

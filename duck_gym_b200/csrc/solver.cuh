@@ -138,7 +138,11 @@ struct StepArgs {
   const void *mass = nullptr, *inertia = nullptr, *friction = nullptr;
 };
 
-template <class R, int T> struct Solver {
+// P = false: a model without body-collision pairs (its colours never change
+// and every contact is a ground contact); the body-pair code is compiled out
+// of that instantiation.
+template <class R, int T, bool P = true> struct Solver {
+  __device__ __forceinline__ bool pairs() const { return P && m->np > 0; }
   static constexpr int kTeams = 32 / T;
   static constexpr int kPerLane = (kMaxBodies + T - 1) / T;   // bodies per lane in lane-per-body loops
   // Lanes that share one body's block update in the Gauss-Seidel sweep: with
@@ -285,7 +289,7 @@ template <class R, int T> struct Solver {
       r[0] = R(metaBody(meta)); r[1] = R(metaShape(meta)); r[2] = R(cfeat(c)); r[3] = R(other);
       r[4] = R(metaOtherShape(meta)); r[5] = R(metaStick(meta) ? 1 : 0);
       r[6] = s[cLocal]; r[7] = s[cLocal + 1]; r[8] = s[cLocal + 2];
-      if (other < 0) {
+      if (!P || other < 0) {
         r[9] = s[cAnchor]; r[10] = s[cAnchor + 1]; r[11] = s[cAnchor + 2];
         r[12] = r[13] = r[14] = R(0);
         r[15] = R(1); r[16] = R(0); r[17] = R(0); r[18] = R(0); r[19] = R(1); r[20] = R(0);
@@ -494,7 +498,7 @@ template <class R, int T> struct Solver {
     base = base < L.cap ? base : L.cap;
     team.sync();
     if (team.lane == 0) I[iGround] = base;
-    if (m->np > 0) base = detectPairs(base, prevCount);
+    if (pairs()) base = detectPairs(base, prevCount);
     if (team.lane == 0) I[iCount] = base;
     team.sync();
     // Per-body masks of the contacts touching each body (list order).
@@ -796,7 +800,7 @@ template <class R, int T> struct Solver {
     const int body = metaBody(meta), other = metaOther(meta);
     const SV c = contact(ci);
     V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
-    if (other < 0) {
+    if (!P || other < 0) {
       V3<R> ra = matVec(Rb, local);
       V3<R> C = x + ra - V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]};
       C.z -= alpha * c[cC0];
@@ -988,7 +992,7 @@ template <class R, int T> struct Solver {
     V3<R> local{c[cLocal], c[cLocal + 1], c[cLocal + 2]};
     V3<R> ra = matVec(rot(body), local);
     V3<R> C;
-    if (other < 0) {
+    if (!P || other < 0) {
       C = ld3(L.X + 3 * body) + ra - V3<R>{c[cAnchor], c[cAnchor + 1], c[cAnchor + 2]};
     } else {
       const SV bs = S + (L.CB + 9 * (ci - nGround));
@@ -1023,7 +1027,7 @@ template <class R, int T> struct Solver {
     const R h = m->dt, alpha = m->alpha, gamma = m->gamma;
     diag = {R(0), R(0), R(0), 0, 0, false};
     detectContacts();
-    if (m->np > 0) buildColorLists();
+    if (pairs()) buildColorLists();
     if (I[iFailed]) {
       storeContacts();
       return false;
@@ -1089,14 +1093,14 @@ template <class R, int T> struct Solver {
       setPose(b, xp, qp);
     }
     team.sync();
-    const int colorCount = m->np > 0 ? I[iColors] : 2;
+    const int colorCount = pairs() ? I[iColors] : 2;
     const R tol = m->tolerance;
     const int iterations = m->iterations;
     for (int it = 0; it < iterations; ++it) {
       R maxUpdate = R(0);
       for (int color = 0; color < colorCount; ++color) {
         int begin, end;
-        if (m->np > 0) {
+        if (pairs()) {
           begin = I[L.colorStart + color];
           end = I[L.colorStart + color + 1];
         } else {
@@ -1115,7 +1119,7 @@ template <class R, int T> struct Solver {
             adjEnd = sc.z;
             role = sc.w;
           } else if (slot < end) {
-            bi = m->np > 0 ? I[L.colorList + slot] : ldg(m->colorBody[slot]);
+            bi = pairs() ? I[L.colorList + slot] : ldg(m->colorBody[slot]);
             adjBegin = ldg(m->csrOffset[bi]);
             adjEnd = ldg(m->csrOffset[bi + 1]);
           }
@@ -1252,7 +1256,7 @@ template <class R, int T> struct Solver {
 
 // One launch advances every environment: target/forces (step) or motor/forces
 // (step_motor), then `substeps` physics steps with all state on chip.
-template <class R, int T>
+template <class R, int T, bool P>
 __global__ void __launch_bounds__(32, T >= 16 ? 14 : 1) advanceKernel(const DevModel<R> *__restrict__ model,
                                                     const R *__restrict__ points, R *records,
                                                     int recordStride, int count, const __grid_constant__ Layout L,
@@ -1265,11 +1269,11 @@ __global__ void __launch_bounds__(32, T >= 16 ? 14 : 1) advanceKernel(const DevM
   // Teams are interleaved word by word: team t owns words t, t + teams, ...
   R *teamBase = reinterpret_cast<R *>(smemRaw) + team;
   R *rec = records + size_t(env) * recordStride;
-  Solver<R, T> s(model, points, teamBase, rec, L);
+  Solver<R, T, P> s(model, points, teamBase, rec, L);
   if (args.mass) s.envMass = static_cast<const R *>(args.mass) + size_t(env) * model->nb;
   if (args.inertia) s.envInertia = static_cast<const R *>(args.inertia) + size_t(env) * model->nb * 3;
   if (args.friction) s.envFriction = static_cast<const R *>(args.friction) + size_t(env) * model->ns;
-  const typename Solver<R, T>::SV S = s.S;
+  const typename Solver<R, T, P>::SV S = s.S;
   const int nj = model->nj;
   const int lane = s.team.lane;
   const R *forces = static_cast<const R *>(args.forces) + 3 * size_t(env);
@@ -1301,7 +1305,7 @@ __global__ void __launch_bounds__(32, T >= 16 ? 14 : 1) advanceKernel(const DevM
       s.I[iFailed] = failed;
     }
     s.team.sync();
-    typename Solver<R, T>::Diag d{R(0), R(0), R(0), 0, 0, true};
+    typename Solver<R, T, P>::Diag d{R(0), R(0), R(0), 0, 0, true};
     bool ran = !failed;
     if (ran) s.advance(1, kp, limit, d);
     s.team.sync();
@@ -1337,7 +1341,7 @@ __global__ void __launch_bounds__(32, T >= 16 ? 14 : 1) advanceKernel(const DevM
     s.I[iFailed] = 0;
   }
   s.team.sync();
-  typename Solver<R, T>::Diag d;
+  typename Solver<R, T, P>::Diag d;
   s.advance(args.substeps, kp, limit, d);
   s.team.sync();
   s.store(kp, limit);
