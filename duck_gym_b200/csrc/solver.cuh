@@ -1053,17 +1053,24 @@ template <class R, int T, bool P = true> struct Solver {
     team.sync();
     // Predictor (kernel.cuh:965-976), one lane per body.  The predicted pose
     // takes over the velocity slots of the body.  x0 and q0 wait for velocity
-    // recovery (the same lane, the same body) in the body's pose slots of the
-    // record, which nothing reads before store() rewrites them at the end of
-    // the call: held in registers they would stay live through every sweep.
+    // recovery (the same lane, the same body) in registers when the model has
+    // no body pairs; the pair instantiation, short of registers, parks them in
+    // the body's pose slots of the record, which nothing reads before store()
+    // rewrites them at the end of the call.
+    V3<R> x0r[P ? 1 : kPerLane];
+    Q4<R> q0r[P ? 1 : kPerLane];
 #pragma unroll
     for (int k = 0; k < kPerLane; ++k) {
       const int b = team.lane + k * T;
       if (b >= nb) continue;
       const V3<R> x = ld3(L.X + 3 * b);
       const Q4<R> q = quat(b);
-      R *r0 = rec + kRecHeader + kRecBody * b;
-      r0[0] = x.x; r0[1] = x.y; r0[2] = x.z; r0[3] = q.w; r0[4] = q.x; r0[5] = q.y; r0[6] = q.z;
+      if constexpr (P) {
+        R *r0 = rec + kRecHeader + kRecBody * b;
+        r0[0] = x.x; r0[1] = x.y; r0[2] = x.z; r0[3] = q.w; r0[4] = q.x; r0[5] = q.y; r0[6] = q.z;
+      } else {
+        x0r[k] = x; q0r[k] = q;
+      }
       const R mass = massOf(b);
       if (mass == R(0)) continue;
       V3<R> in = inertiaOf(b);
@@ -1189,9 +1196,16 @@ template <class R, int T, bool P = true> struct Solver {
       const int b = team.lane + k * T;
       if (b >= nb || !(ldg(m->mass[b]) > R(0))) continue;
       V3<R> x = ld3(L.X + 3 * b);
-      const R *r0 = rec + kRecHeader + kRecBody * b;
-      const V3<R> x0{r0[0], r0[1], r0[2]};
-      const Q4<R> q0{r0[3], r0[4], r0[5], r0[6]};
+      V3<R> x0;
+      Q4<R> q0;
+      if constexpr (P) {
+        const R *r0 = rec + kRecHeader + kRecBody * b;
+        x0 = {r0[0], r0[1], r0[2]};
+        q0 = {r0[3], r0[4], r0[5], r0[6]};
+      } else {
+        x0 = x0r[k];
+        q0 = q0r[k];
+      }
       V3<R> v = (x - x0) * (R(1) / h);
       V3<R> w = fqlog(qmul(quat(b), conj(q0))) * (R(1) / h);
       SV vw = S + (L.XQP + 7 * b);
