@@ -1,4 +1,5 @@
-"""Benchmark of the batched AVBD environment step.
+"""Benchmark of the batched AVBD environment step: the pure-engine step of
+the synthetic biped.
 
 Workload: the seed-0 synthetic biped, 4096 environments per GPU, dt 5 ms,
 4 substeps per control step, 10 AVBD iterations, fp32, PD targets HOME +
@@ -10,14 +11,18 @@ kernel launch advancing every environment 4 physics steps.
 Metric: physics env-steps/s = envs x substeps x K / device seconds (the
 reference's formula, scripts/benchmark_engines.py:551), summed over ranks and
 divided by the slowest rank's time.  The L2 cache is flushed (256 MiB write)
-between timed steps, outside the timed events.
+between timed steps, outside the timed events.  After the K steps the
+reference's own method runs beside it (median of 5 trials x 200 steps), then
+the end-to-end pass through the public API with host copies every step.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
 
-``--workload config3`` and ``--workload config5`` time the other BASELINE
-configurations (extensions beyond the reference; see run_extended); the
-default, config 2, is the headline line.
+``--workload config3`` (91-pair self-contact BAM env, 16384 envs per GPU),
+``--workload config4`` (PPO rollout and update) and ``--workload config5``
+(65536 domain-randomised envs per GPU at 20 iterations) time the larger
+workloads (see run_extended and run_ppo); the default, the 4096-env
+pure-engine step, is the headline line.
 """
 
 from __future__ import annotations
@@ -45,6 +50,9 @@ ITERATIONS = 10
 DT = 0.005
 SETTLE = 200
 NOISE = 0.05
+TRIALS = 5           # the reference's method: median of 5 trials ...
+TRIAL_STEPS = 200    # ... of 200 control steps each
+FLOP_STEPS = 20      # control steps the flop count follows from the timed states
 METRIC = "physics env-steps/s"
 UNIT = "env-steps/s"
 
@@ -59,7 +67,7 @@ def workload(args):
         "settle_steps": SETTLE,
         "kp": None,
         "torque_limit": None,
-        "l2": "flushed between timed steps (256 MiB write, outside the timed events)",
+        "l2": "GPU: flushed between timed steps (256 MiB write, outside the timed events); CPU arm: host run",
         "parallelism": f"env shards x{args.gpus}, no physics communication",
     }
 
@@ -78,112 +86,182 @@ def fixed_targets(meta, envs, seed):
     return (home + rng.normal(0, NOISE, (envs, home.size))).astype(np.float32)
 
 
+REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+
 class ClockSampler:
-    """nvidia-smi clock / throttle samples taken while the timed region runs."""
+    """SM clock and throttle-reason samples taken while the timed region runs.
+
+    Reads NVML in-process every 5 ms (read-only queries), so even a timed
+    region of a few milliseconds holds samples; falls back to an nvidia-smi
+    loop at 100 ms where NVML cannot be loaded."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD = 0.005
 
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.lines = []      # (monotonic receive time, csv line)
+        self.thread = None
+        self.running = False
+        self.lines = []      # (monotonic time, sm MHz, max MHz, power W, set of reasons)
         self.window = None   # (start, end) of the timed region
+        self.source = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def start(self):
         """Start sampling; returns once the first sample has arrived."""
         try:
+            nvml, handle = self._nvml_handle()
+            bits = {"hw_slowdown": nvml.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nvml.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nvml.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nvml.nvmlClocksEventReasonSwPowerCap}
+            sm_max = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
+
+            def poll():
+                while self.running:
+                    try:
+                        sm = float(nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM))
+                        mask = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                        power = nvml.nvmlDeviceGetPowerUsage(handle) / 1e3
+                    except Exception:
+                        break
+                    self.lines.append((time.monotonic(), sm, sm_max, power,
+                                       {name for name, bit in bits.items() if mask & bit}))
+                    time.sleep(self.PERIOD)
+
+            self.running = True
+            self.source = "NVML in-process, every 5 ms"
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+        except Exception:
+            self._start_smi()
+        deadline = time.monotonic() + 10
+        while not self.lines and time.monotonic() < deadline:
+            time.sleep(0.01)
+
+    def _start_smi(self):
+        try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.source = "nvidia-smi every 100 ms"
+
+            def read():
+                for line in self.proc.stdout:
+                    parts = [p.strip() for p in line.split(",")]
+                    try:
+                        self.lines.append((time.monotonic(), float(parts[1]), float(parts[2]), float(parts[3]),
+                                           {n for n, f in zip(REASONS, parts[5:9]) if f.lower() == "active"}))
+                    except (ValueError, IndexError):
+                        continue
+
+            self.thread = threading.Thread(target=read, daemon=True)
             self.thread.start()
-            deadline = time.monotonic() + 10
-            while not self.lines and time.monotonic() < deadline:
-                time.sleep(0.05)
         except OSError:
             self.proc = None
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append((time.monotonic(), line.strip()))
-
     def stop(self):
+        self.running = False
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self.thread:
             self.thread.join(timeout=5)
 
-    def summary(self):
-        """Samples received while the timed region ran (plus one period)."""
+    def summary(self, window=None):
+        """Samples taken while the timed region (or `window`) ran."""
         sm, reasons, sm_max, power = [], set(), None, []
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        start, end = self.window or (-1e30, 1e30)
-        for when, line in self.lines:
-            if not (start <= when <= end + 0.15):
-                continue
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                sm_max = float(parts[2])
-                power.append(float(parts[3]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
+        start, end = window or self.window or (-1e30, 1e30)
+        for when, mhz, top, watts, active in self.lines:
+            if start <= when <= end:
+                sm.append(mhz)
+                sm_max = top
+                power.append(watts)
+                reasons |= active
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": self.source}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": sm_max, "reasons": sorted(reasons),
-                "samples": len(sm), "power_w_max": max(power) if power else None}
+                "samples": len(sm), "power_w_max": max(power) if power else None, "source": self.source}
 
 
-def count_flops(model, meta, envs, steps):
+def count_flops(model, meta, targets, records, steps):
     """Algorithmic flops per physics env-step, counted by the CPU oracle's
-    counting scalar on the same workload (HOME start, fixed targets)."""
+    counting scalar on the states the timed region starts from: `records` are
+    the envs' portable records exported right before the timed steps, advanced
+    `steps` control steps with the same `targets` [envs, J]."""
     from oracle.oracle import count_ops
 
-    targets = np.repeat(fixed_targets(meta, envs, 0)[None], steps, axis=0)
-    c = count_ops(model, np.asarray(meta["home"], np.float32), targets, np.zeros((envs, 3), np.float32), DT,
-                  ITERATIONS, SUBSTEPS, meta["kp"], meta["torque_limit"])
+    envs = targets.shape[0]
+    c = count_ops(model, np.asarray(meta["home"], np.float32), np.repeat(targets[None], steps, axis=0),
+                  np.zeros((envs, 3), np.float32), DT, ITERATIONS, SUBSTEPS, meta["kp"], meta["torque_limit"],
+                  records=records, threads=min(64, os.cpu_count() or 1))
     flops = c["add"] + c["mul"] + c["div"] + c["sqrt"]
     transcendental = c["sin"] + c["cos"] + c["tan"] + c["atan2"] + c["hypot"] + c["remainder"]
     n = c["physics_steps"]
     return {"flops_per_env_step": flops / n, "transcendentals_per_env_step": transcendental / n,
-            "gs_iterations_per_env_step": c["gs_iterations"] / n, "sample": f"{envs} envs x {steps} control steps"}
+            "gs_iterations_per_env_step": c["gs_iterations"] / n,
+            "sample": f"all {envs} envs from the timed region's starting states x {steps} control steps"}
 
 
-def cpu_baseline(model, meta, seconds=15.0):
-    """The reference's own CPU solver (oracle/_ref CpuBatch32) on this host's
-    cores, else the CPU restatement; bounded to about `seconds` of work."""
+def reference_batch(model, envs, cores):
+    """The reference's own CPU solver (oracle/_ref CpuBatch32), else the CPU
+    restatement, with the kind string for the JSON line."""
     from oracle.oracle import OracleBatch, reference_module
 
     ref = reference_module()
-    cores = min(64, os.cpu_count() or 1)
-    envs = 4096
-    kind = "reference" if ref is not None else "port"
     if ref is not None:
-        batch = ref.CpuBatch32(str(model), envs, DT, ITERATIONS, cores)
-    else:
-        batch = OracleBatch(model, envs, DT, ITERATIONS, threads=cores)
+        return ref.CpuBatch32(str(model), envs, DT, ITERATIONS, cores), "reference"
+    return OracleBatch(model, envs, DT, ITERATIONS, threads=cores), "port"
+
+
+def cpu_settled(model, meta, envs, cores, settle=SETTLE):
+    """A CPU batch on the bench workload after the same untimed settle steps
+    as the GPU arm (HOME start, fixed targets)."""
+    batch, kind = reference_batch(model, envs, cores)
     target = fixed_targets(meta, envs, 0)
     forces = np.zeros((envs, 3), np.float32)
+    for _ in range(settle):
+        batch.step(target, forces, SUBSTEPS, meta["kp"], meta["torque_limit"])
+    return batch, kind, target, forces
+
+
+def cpu_baseline(model, meta, seconds=12.0, envs=1024):
+    """The reference's own CPU solver (oracle/_ref CpuBatch32) on this host's
+    cores, else the CPU restatement, on a bounded sample of the workload: the
+    first `envs` environments' targets, settled like the GPU arm, then timed
+    for about `seconds` (median of 5 trials)."""
+    cores = min(64, os.cpu_count() or 1)
+    batch, kind, target, forces = cpu_settled(model, meta, envs, cores)
     t0 = time.perf_counter()
     batch.step(target, forces, SUBSTEPS, meta["kp"], meta["torque_limit"])
     first = time.perf_counter() - t0
-    steps = max(1, min(200, int(seconds / max(first, 1e-3))))
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        batch.step(target, forces, SUBSTEPS, meta["kp"], meta["torque_limit"])
-    elapsed = time.perf_counter() - t0
-    return {"value": envs * SUBSTEPS * steps / elapsed, "unit": UNIT, "cores": cores, "kind": kind,
-            "sample": f"{envs} envs x {steps} control steps ({SUBSTEPS} substeps), after 1 untimed step, wall clock"}
+    steps = max(1, min(100, int(seconds / 5 / max(first, 1e-3))))
+    values = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            batch.step(target, forces, SUBSTEPS, meta["kp"], meta["torque_limit"])
+        values.append(envs * SUBSTEPS * steps / (time.perf_counter() - t0))
+    return {"value": statistics.median(values), "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{envs} envs after {SETTLE} settle steps, median of 5 trials x {steps} control steps "
+                      f"({SUBSTEPS} substeps), wall clock"}
 
 
 def traffic_from_profile():
@@ -202,23 +280,15 @@ def traffic_from_profile():
 
 def reference_arm(args, rank, world):
     """--impl reference: the reference's CPU solver (oracle/_ref, else the
-    oracle port) on the host cores, same workload and metric."""
+    oracle port) on all host cores, on the same workload, settled the same
+    200 steps, then W warm-up and K timed control steps (wall clock)."""
     if rank != 0:
         return
     with tempfile.TemporaryDirectory() as d:
         model, meta = make_model(d)
-        from oracle.oracle import OracleBatch, reference_module
-
-        ref = reference_module()
         cores = min(64, os.cpu_count() or 1)
         envs = min(args.envs, 4096)
-        kind = "reference" if ref is not None else "port"
-        if ref is not None:
-            batch = ref.CpuBatch32(str(model), envs, DT, ITERATIONS, cores)
-        else:
-            batch = OracleBatch(model, envs, DT, ITERATIONS, threads=cores)
-        target = fixed_targets(meta, envs, 0)
-        forces = np.zeros((envs, 3), np.float32)
+        batch, kind, target, forces = cpu_settled(model, meta, envs, cores)
         for _ in range(args.warmup):
             batch.step(target, forces, SUBSTEPS, meta["kp"], meta["torque_limit"])
         t0 = time.perf_counter()
@@ -227,15 +297,16 @@ def reference_arm(args, rank, world):
         elapsed = time.perf_counter() - t0
         value = envs * SUBSTEPS * args.steps / elapsed
         cfg = workload(args)
-        cfg.update(kp=meta["kp"], torque_limit=meta["torque_limit"], envs_per_gpu=envs,
-                   settle_steps=0, l2="host run")
+        cfg.update(kp=meta["kp"], torque_limit=meta["torque_limit"], envs_per_gpu=envs)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * elapsed / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded biped, no dataset)",
+            "config": cfg,
             "impl": "reference",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
-                             "sample": f"{envs} envs x {args.steps} control steps after {args.warmup} warm-up"},
+                             "sample": f"{envs} envs after {SETTLE} settle + {args.warmup} warm-up steps, "
+                                       f"{args.steps} control steps timed"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
         print(json.dumps(line), flush=True)
@@ -245,13 +316,13 @@ COMMAND_RANGES = [[-0.3, 0.3], [-0.3, 0.3], [-1.0, 1.0]]
 
 
 def run_ppo(args, rank, world, local, device):
-    """full RL rollout plus PPO update.  4096 BamEnv envs
+    """Full RL rollout plus PPO update.  4096 BamEnv envs
     per GPU (the synthetic bundle, dt 5 ms, decimation 4, 10 iterations) on a
     velocity-command task, commands U[-0.3,0.3] m/s in x/y and U[-1,1] rad/s
     in yaw; actor MLP 61-512-256-128-14 ELU under bf16 autocast (the actor
     observation has 51 live entries -- angular velocity, gravity, joint
     positions and velocities, last action, command -- plus the reference's 10
-    zero pads; BASELINE's "48-dim" does not add up to its own list); 24-step
+    zero pads; a 48-dim layout does not add up to that list of terms); 24-step
     rollouts, 5 epochs x 4 minibatches; gradients averaged over the ranks by
     bucketed NCCL all-reduces overlapped with backward.  One step = one PPO
     iteration; value = envs x 24 x 4 physics steps per iteration x ranks /
@@ -324,8 +395,9 @@ def run_ppo(args, rank, world, local, device):
 
 
 def run_extended(args, rank, world, local, device):
-    """BASELINE configs 3 and 5 on the synthetic biped (both beyond the
-    reference's envelope: 91 body-collision pairs; per-env parameters).
+    """The self-contact and domain-randomised workloads on the synthetic biped
+    (both beyond the reference's envelope: 91 body-collision pairs; per-env
+    parameters).
 
     config3: 16384 envs per GPU, self-contact on (all 91 non-adjacent link
       pairs), the BAM servo of the synthetic bundle (4 N m/rad, 0.1 N m s/rad,
@@ -493,15 +565,27 @@ def main():
             batch.step(target, forces, SUBSTEPS, kp, limit)
         for _ in range(args.warmup):
             batch.step(target, forces, SUBSTEPS, kp, limit)
+        # The states the timed region starts from, for the flop count.
+        start_records = batch.export_records().cpu().numpy() if rank == 0 else None
         flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)  # 256 MiB > L2
         stream = torch.cuda.current_stream(device)
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
 
         def barrier():
             if world > 1:
                 dist.barrier()
             torch.cuda.synchronize(device)
+
+        def timed(steps):
+            """Per-step device times (ms) of `steps` steps, L2 flushed between
+            steps outside the events, on the launching stream."""
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            for k in range(steps):
+                flush.zero_()
+                starts[k].record(stream)
+                batch.step(target, forces, SUBSTEPS, kp, limit)
+                ends[k].record(stream)
+            return starts, ends
 
         clocks = ClockSampler(local)
         clocks.start()
@@ -509,15 +593,10 @@ def main():
         barrier()
         wall0 = time.perf_counter()
         t_start = time.monotonic()
-        for k in range(args.steps):
-            flush.zero_()
-            starts[k].record(stream)
-            batch.step(target, forces, SUBSTEPS, kp, limit)
-            ends[k].record(stream)
+        starts, ends = timed(args.steps)
         barrier()
-        clocks.window = (t_start, time.monotonic())
+        t_end = time.monotonic()
         wall = time.perf_counter() - wall0
-        clocks.stop()
         launches = batch.launches - launches0
         kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
         device_s = sum(kernel_ms) / 1e3
@@ -525,12 +604,27 @@ def main():
         total_steps = envs * SUBSTEPS * args.steps * world
         value = total_steps / slowest
 
-        # End to end through the public API: pinned host targets in, one
-        # step, state() snapshot, diagnostics back to the host, every step.
+        # The reference's own method beside it (benchmark_engines.py:510-551):
+        # 5 trials of TRIAL_STEPS steps, median, max over ranks per trial.
+        trial_values = []
+        for _ in range(TRIALS):
+            barrier()
+            ts, te = timed(TRIAL_STEPS)
+            barrier()
+            trial_s = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(ts, te)) / 1e3, device)
+            trial_values.append(envs * SUBSTEPS * TRIAL_STEPS * world / trial_s)
+
+        # End to end through the public API, every step: the step's targets
+        # and forces copied in from pinned host memory, one step, the full
+        # state() snapshot (bodies, joints, diagnostics) copied back to pinned
+        # host memory.
         host_in = torch.from_numpy(target_host).pin_memory()
         host_forces = torch.zeros(envs, 3).pin_memory()
-        host_out = torch.empty(envs, 6).pin_memory()
-        e2e_steps = max(10, args.steps // 2)
+        nb, nj = batch.num_bodies, batch.num_joints
+        host_bodies = torch.empty(envs, nb, 13).pin_memory()
+        host_joints = torch.empty(envs, nj, 2).pin_memory()
+        host_diag = torch.empty(envs, 6).pin_memory()
+        e2e_steps = max(10, args.steps)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
@@ -539,17 +633,21 @@ def main():
             tin = host_in.to(device, non_blocking=True)
             fin = host_forces.to(device, non_blocking=True)
             batch.step(tin, fin, SUBSTEPS, kp, limit)
-            diag = batch.state()[2]
-            host_out.copy_(diag, non_blocking=True)
+            b, j, g = batch.state()
+            host_bodies.copy_(b, non_blocking=True)
+            host_joints.copy_(j, non_blocking=True)
+            host_diag.copy_(g, non_blocking=True)
         e1.record(stream)
         barrier()
+        clocks.window = (t_start, time.monotonic())
+        clocks.stop()
         e2e_value = envs * SUBSTEPS * e2e_steps * world / max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
-        failed_fraction = float((host_out[:, 5] > 0).float().mean())
+        failed_fraction = float((host_diag[:, 5] > 0).float().mean())
 
         line = None
         if rank == 0:
             peak = fp32_peak_tflops(local)
-            flops = count_flops(model, meta, 64, 50)
+            flops = count_flops(model, meta, target_host, start_records, min(args.steps, FLOP_STEPS))
             mean_kernel_s = statistics.mean(kernel_ms) / 1e3
             achieved = flops["flops_per_env_step"] * envs * SUBSTEPS / mean_kernel_s / 1e12
             state_bytes = batch.record_length * 4  # record read + written per launch (upper bound)
@@ -570,21 +668,27 @@ def main():
                 "roofline": {
                     "bound": "fp32", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                     "traffic": traffic,
-                    "kernel": "advanceKernel<float,8>",
+                    "kernel": "advanceKernel<float,8,false>",
                     "peak_source": "measured: FP32 FMA probe on this GPU (duck_fp32_peak), 2 flops per FMA",
                     "flops_per_env_step": flops["flops_per_env_step"],
                     "flops_source": "oracle counting scalar (+,-,*,/,sqrt), " + flops["sample"],
                     "transcendentals_per_env_step": flops["transcendentals_per_env_step"],
+                    "gs_iterations_per_env_step": flops["gs_iterations_per_env_step"],
                     "hbm": {"algorithmic_bytes_per_launch": hbm_algorithmic,
                             "achieved_gbs": hbm_algorithmic / mean_kernel_s / 1e9, "peak_gbs": hbm_peak,
                             "frac": hbm_algorithmic / mean_kernel_s / 1e9 / hbm_peak,
                             "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback 6650 GB/s"},
                 },
-                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": envs * (14 + 3) * 4,
-                        "d2h_bytes_per_step": envs * 6 * 4,
-                        "path": "CudaBatch.step + CudaBatch.state() with pinned host targets/forces in and diag out"},
+                "trials": {"count": TRIALS, "steps_each": TRIAL_STEPS, "median": statistics.median(trial_values),
+                           "values": trial_values, "method": "per-step CUDA events summed per trial, L2 flushed "
+                                                             "between steps, max over ranks"},
+                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": envs * (nj + 3) * 4,
+                        "d2h_bytes_per_step": envs * (nb * 13 + nj * 2 + 6) * 4, "steps": e2e_steps,
+                        "path": "CudaBatch.step + CudaBatch.state(): pinned host targets/forces in, bodies, joints "
+                                "and diag out, every step"},
                 "gpu_launches": launches,
-                "clocks": clocks.summary(),
+                "clocks": clocks.summary((t_start, t_end)),
+                "clocks_all_regions": clocks.summary(),
                 "wall_s": wall,
                 "failed_env_fraction": failed_fraction,
             }

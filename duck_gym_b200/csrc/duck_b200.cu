@@ -499,14 +499,16 @@ int duck_batch_reference(duck_batch *b, const void *target, const void *forces, 
 //
 // duck_batch_reference takes its one-environment scratch record and staging
 // buffers from cudaMalloc.  Some callers cannot allocate device memory at the
-// moment they want this check: code running while a stream is being captured
-// into a CUDA graph (allocation is not capturable), code under a memory pool
-// or budget that forbids raw cudaMalloc, and control loops that cannot afford
-// the device-wide synchronisation cudaMalloc/cudaFree imply.  This variant
+// moment they want this check: a host framework whose caching allocator owns
+// the device memory and forbids raw cudaMalloc next to it, a process running
+// under a fixed device-memory budget, or a real-time control loop that must
+// not take the implicit synchronisation of cudaMalloc/cudaFree.  This variant
 // keeps the scratch in a file-scope device array instead.  Every GPU that
 // loads the library holds the array (kStaticScratchBytes) until exit; all
 // calls share it and it keeps the previous call's contents, so the record is
-// cleared on every call, and calls that overlap on the GPU race.
+// cleared on every call, and calls that overlap on the GPU race.  The call is
+// synchronous like duck_batch_reference: it copies from and to host memory
+// with cudaMemcpy and works on the legacy default stream.
 static constexpr size_t kStaticScratchBytes = 32 * 1024;
 static __device__ __align__(256) unsigned char duckStaticScratch[kStaticScratchBytes];
 
@@ -515,8 +517,11 @@ std::mutex staticScratchMutex;
 void *staticScratchAddress[64] = {};
 
 // Device address of duckStaticScratch on `device` (current), resolved once per
-// device: host code cannot use the symbol itself, which names a host-side
-// stand-in, not device memory.
+// device at its first call: host code cannot use the symbol itself, which
+// names a host-side stand-in, not device memory.  The cached address belongs
+// to the device's primary context: a cudaDeviceReset of that device (which
+// also invalidates every batch on it) leaves it stale, so a process must not
+// use this entry point on a device after resetting it.
 void *staticScratch(int device) {
   require(device >= 0 && device < 64, "Device index out of range");
   std::lock_guard<std::mutex> lock(staticScratchMutex);
@@ -529,18 +534,25 @@ void *staticScratch(int device) {
 }
 
 template <class R>
-void referenceStatic(const duck_batch *b, char *scratch, size_t recordBytes, const StepArgs &args, char *dBodies,
+void referenceStatic(duck_batch *b, char *scratch, size_t recordBytes, const StepArgs &stepArgs, char *dBodies,
                      char *dJoints, char *dDiag) {
   const DevModel<R> *m = static_cast<const DevModel<R> *>(b->devModel);
   const R *pts = static_cast<const R *>(b->points);
   R *rec = reinterpret_cast<R *>(scratch);
   const int stride = b->recordStride;
+  // The one-environment record is environment 0 of the parameter arrays, as
+  // in duck_batch_reference's private batch.
+  StepArgs args = stepArgs;
+  args.mass = b->envMass;
+  args.inertia = b->envInertia;
+  args.friction = b->envFriction;
   check(cudaMemset(scratch, 0, recordBytes), "cudaMemset scratch record");
   resetKernel<R><<<1, 128>>>(m, rec, stride, 1, nullptr, nullptr, nullptr, 0);
   withAdvance<R>(b, [&](auto kernel) { kernel<<<1, 32, b->smemPerBlock>>>(m, pts, rec, stride, 1, b->layout, args); });
-  snapshotKernel<R><<<1, 64>>>(m, rec, stride, 1, reinterpret_cast<R *>(dBodies), reinterpret_cast<R *>(dJoints),
+  snapshotKernel<R><<<blocksFor(b->nb + b->nj + 1, 256), 256>>>(m, rec, stride, 1, reinterpret_cast<R *>(dBodies), reinterpret_cast<R *>(dJoints),
                                reinterpret_cast<R *>(dDiag));
   check(cudaGetLastError(), "static reference launch");
+  b->launches += 3;
 }
 }  // namespace
 

@@ -120,22 +120,28 @@ int duck_batch_reference(duck_batch *batch, const void *target, const void *forc
                          double kp, double limit, void *bodies, void *joints, void *diag);
 
 /* No counterpart in the reference: an allocation-free duck_batch_reference.
- * Same arguments, same results.  duck_batch_reference takes its scratch (a
- * one-environment state record plus staging for inputs and outputs) from
- * cudaMalloc; this entry point calls no cudaMalloc, cudaFree or allocating
- * library routine.  It is for callers that cannot allocate device memory:
- * code running while a stream is captured into a CUDA graph, code under a
- * memory pool or budget that forbids raw cudaMalloc, and control loops that
- * cannot take the device-wide synchronisation that cudaMalloc/cudaFree imply.
+ * Same arguments, same results (per-environment parameters included: the one
+ * environment uses environment 0's values, as duck_batch_reference does).
+ * duck_batch_reference takes its scratch (a one-environment state record plus
+ * staging for inputs and outputs) from cudaMalloc; this entry point calls no
+ * cudaMalloc, cudaFree or allocating library routine.  It is for callers that
+ * cannot allocate device memory when they want this check: a host framework
+ * whose caching allocator owns the device memory and forbids raw cudaMalloc
+ * beside it, a process held to a fixed device-memory budget, and real-time
+ * control loops that must not take the implicit synchronisation of
+ * cudaMalloc/cudaFree.  It gives no allocation and nothing more: like
+ * duck_batch_reference it is synchronous, copies from and to host memory with
+ * cudaMemcpy and runs on the legacy default stream.
  * Its scratch is a file-scope device array of 32 KiB that every GPU loading
  * the library holds until exit; models whose record and staging need more are
  * rejected with DUCK_EINVAL and a message giving both sizes (the seed biped
  * needs 10 KiB in fp32, 20 KiB in fp64).  The first call on a device resolves
- * the array's device address; make that first call before any stream
- * capture.  All calls share the array and it keeps the previous call's
- * contents (each call clears the record before use), so calls that overlap on
- * the GPU race: serialise them.  Inputs and outputs are host pointers, as for
- * duck_batch_reference. */
+ * the array's device address with that device current and caches it for the
+ * process; after a cudaDeviceReset of the device the cached address is stale,
+ * so do not use this entry point on a device after resetting it.  All calls
+ * share the array and it keeps the previous call's contents (each call clears
+ * the record before use), so calls that overlap on the GPU race: serialise
+ * them.  Inputs and outputs are host pointers, as for duck_batch_reference. */
 int duck_batch_reference_static(duck_batch *batch, const void *target, const void *forces,
                                 int substeps, double kp, double limit, void *bodies, void *joints,
                                 void *diag);

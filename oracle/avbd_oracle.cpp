@@ -24,6 +24,7 @@
 
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <thread>
 
 using namespace avbd_oracle;
@@ -65,6 +66,49 @@ template <class F> void parallel(int n, int threads, F &&work) {
     pool.emplace_back([&, w] { for (int e = w; e < n; e += workers) work(e); });
   for (int e = 0; e < n; e += workers) work(e);
   for (auto &t : pool) t.join();
+}
+
+// Loads one portable record (the layout exportEnv writes) into an env of any
+// scalar type: the oracle batch's own, or the counting scalar's.
+template <class S, class Src> void loadRecord(S &s, const Src *o, int bodies, int joints, int bound) {
+  using Item = typename std::decay_t<decltype(s.contacts)>::value_type;
+  s.failed = int(o[0]);
+  int count = int(o[1]);
+  if (count < 0 || count > bound) throw std::invalid_argument("contact count out of range");
+  s.diagnostics = {};
+  s.diagnostics.jointError = o[2];
+  s.diagnostics.penetration = o[3];
+  s.diagnostics.contacts = int(o[4]);
+  s.diagnostics.converged = o[5] != Src(0);
+  s.diagnostics.axisError = o[6];
+  s.diagnostics.iterations = int(o[7]);
+  const Src *b = o + 8;
+  for (int i = 0; i < bodies; ++i, b += 16) {
+    auto &v = s.bodies[i];
+    v.x = {b[0], b[1], b[2]};
+    v.q = {b[3], b[4], b[5], b[6]};
+    v.v = {b[7], b[8], b[9]};
+    v.w = {b[10], b[11], b[12]};
+    v.force = {b[13], b[14], b[15]};
+  }
+  const Src *j = o + 8 + bodies * 16;
+  for (int i = 0; i < joints; ++i, j += 22) {
+    auto &v = s.joints[i];
+    for (int k = 0; k < 7; ++k) { v.lambda[k] = j[k]; v.penalty[k] = j[7 + k]; }
+    v.lambdaF = j[14]; v.penaltyF = j[15]; v.target = j[16]; v.kp = j[17];
+    v.maxTorque = j[18]; v.torque = j[19]; v.frictionloss = j[20]; v.damping = j[21];
+  }
+  const Src *c = o + 8 + bodies * 16 + joints * 22;
+  s.contacts.assign(count, Item{});
+  for (int i = 0; i < count; ++i, c += 32) {
+    auto &v = s.contacts[i];
+    v.body = int(c[0]); v.shape = int(c[1]); v.feature = int(c[2]); v.other = int(c[3]);
+    v.otherShape = int(c[4]); v.stick = c[5] != Src(0);
+    v.local = {c[6], c[7], c[8]}; v.anchor = {c[9], c[10], c[11]}; v.localB = {c[12], c[13], c[14]};
+    v.tangent1 = {c[15], c[16], c[17]}; v.tangent2 = {c[18], c[19], c[20]}; v.normal = {c[21], c[22], c[23]};
+    v.friction = c[24]; v.c0 = c[25];
+    for (int k = 0; k < 3; ++k) { v.lambda[k] = c[26 + k]; v.penalty[k] = c[29 + k]; }
+  }
 }
 
 template <class R> struct Batch final : BatchBase {
@@ -201,45 +245,7 @@ template <class R> struct Batch final : BatchBase {
     }
   }
   void importEnv(int env, const void *src) override {
-    auto &s = envs.at(env);
-    const R *o = static_cast<const R *>(src);
-    s.failed = int(o[0]);
-    int count = int(o[1]);
-    if (count < 0 || count > bound) throw std::invalid_argument("contact count out of range");
-    s.diagnostics = {};
-    s.diagnostics.jointError = o[2];
-    s.diagnostics.penetration = o[3];
-    s.diagnostics.contacts = int(o[4]);
-    s.diagnostics.converged = o[5] != R(0);
-    s.diagnostics.axisError = o[6];
-    s.diagnostics.iterations = int(o[7]);
-    const R *b = o + 8;
-    for (int i = 0; i < bodies; ++i, b += 16) {
-      auto &v = s.bodies[i];
-      v.x = {b[0], b[1], b[2]};
-      v.q = {b[3], b[4], b[5], b[6]};
-      v.v = {b[7], b[8], b[9]};
-      v.w = {b[10], b[11], b[12]};
-      v.force = {b[13], b[14], b[15]};
-    }
-    const R *j = o + 8 + bodies * 16;
-    for (int i = 0; i < joints; ++i, j += 22) {
-      auto &v = s.joints[i];
-      for (int k = 0; k < 7; ++k) { v.lambda[k] = j[k]; v.penalty[k] = j[7 + k]; }
-      v.lambdaF = j[14]; v.penaltyF = j[15]; v.target = j[16]; v.kp = j[17];
-      v.maxTorque = j[18]; v.torque = j[19]; v.frictionloss = j[20]; v.damping = j[21];
-    }
-    const R *c = o + 8 + bodies * 16 + joints * 22;
-    s.contacts.assign(count, Contact<R>{});
-    for (int i = 0; i < count; ++i, c += 32) {
-      auto &v = s.contacts[i];
-      v.body = int(c[0]); v.shape = int(c[1]); v.feature = int(c[2]); v.other = int(c[3]);
-      v.otherShape = int(c[4]); v.stick = c[5] != R(0);
-      v.local = {c[6], c[7], c[8]}; v.anchor = {c[9], c[10], c[11]}; v.localB = {c[12], c[13], c[14]};
-      v.tangent1 = {c[15], c[16], c[17]}; v.tangent2 = {c[18], c[19], c[20]}; v.normal = {c[21], c[22], c[23]};
-      v.friction = c[24]; v.c0 = c[25];
-      for (int k = 0; k < 3; ++k) { v.lambda[k] = c[26 + k]; v.penalty[k] = c[29 + k]; }
-    }
+    loadRecord(envs.at(env), static_cast<const R *>(src), bodies, joints, bound);
   }
 };
 
@@ -324,12 +330,15 @@ int avbd_oracle_import(void *b, int env, const void *src) {
 
 // Counts the algorithmic floating-point operations of `steps` control steps
 // of the fp32 solver on n envs: targets [steps][n][J] and forces [n][3] are
-// float32.  The run is reset to q = home, roots = 0 first.  out[10] receives
+// float32.  The run starts from `records` ([n][record length] float32
+// portable records, e.g. states exported from a GPU batch) when given, else
+// from a reset to q = home, roots = 0.  out[0..9] receives
 // add, mul, div, sqrt, sin, cos, tan, atan2, hypot, remainder counts; out[10]
 // the number of GS iterations actually executed, out[11] the physics steps.
+// A failed env stops advancing (its remaining steps still count in out[11]).
 int avbd_oracle_count_ops(const char *path, int n, double dt, int iterations, const float *home,
-                          const float *targets, const float *forces, int steps, int substeps,
-                          double kp, double limit, uint64_t *out) {
+                          const float *records, const float *targets, const float *forces, int steps,
+                          int substeps, double kp, double limit, int threads, uint64_t *out) {
   return guarded([&] {
     using T = Tally<float>;
     DModel d = loadDuck(path);
@@ -337,29 +346,50 @@ int avbd_oracle_count_ops(const char *path, int n, double dt, int iterations, co
     const int nj = int(model.joints.size());
     std::vector<Env<T, Tally<double>>> envs(n);
     std::vector<float> roots(6, 0.f);
-    for (auto &e : envs) {
-      e.initialize(&model);
-      e.resetPose(home, roots.data());
+    const int nb = int(model.bodies.size()), bound = contactBound(d);
+    const int length = 8 + 16 * nb + 22 * nj + 32 * bound;
+    for (int e = 0; e < n; ++e) {
+      envs[e].initialize(&model);
+      if (records) loadRecord(envs[e], records + size_t(e) * length, nb, nj, bound);
+      else envs[e].resetPose(home, roots.data());
     }
-    counts() = {};
+    // Envs are independent: `threads` workers take every threads-th env and
+    // run all its steps; each worker's thread-local tally is summed at the end.
+    OpCounts total{};
     uint64_t iters = 0;
-    for (int s = 0; s < steps; ++s)
-      for (int e = 0; e < n; ++e) {
+    std::mutex sum;
+    auto work = [&](int w, int workers) {
+      counts() = {};
+      uint64_t mine = 0;
+      for (int e = w; e < n; e += workers) {
         auto &env = envs[e];
-        if (env.failed) continue;
-        for (int j = 0; j < nj; ++j) {
-          env.joints[j].target = targets[(size_t(s) * n + e) * nj + j];
-          env.joints[j].kp = T(float(kp));
-          env.joints[j].maxTorque = T(float(limit));
-          env.joints[j].torque = model.joints[j].torque;
-          env.joints[j].frictionloss = model.joints[j].frictionloss;
-          env.joints[j].damping = model.joints[j].damping;
+        for (int s = 0; s < steps && !env.failed; ++s) {
+          for (int j = 0; j < nj; ++j) {
+            env.joints[j].target = targets[(size_t(s) * n + e) * nj + j];
+            env.joints[j].kp = T(float(kp));
+            env.joints[j].maxTorque = T(float(limit));
+            env.joints[j].torque = model.joints[j].torque;
+            env.joints[j].frictionloss = model.joints[j].frictionloss;
+            env.joints[j].damping = model.joints[j].damping;
+          }
+          env.bodies[1].force = {T(forces[3 * e]), T(forces[3 * e + 1]), T(forces[3 * e + 2])};
+          env.advance(substeps);
+          mine += env.diagnostics.iterations;
         }
-        env.bodies[1].force = {T(forces[3 * e]), T(forces[3 * e + 1]), T(forces[3 * e + 2])};
-        env.advance(substeps);
-        iters += env.diagnostics.iterations;
       }
-    const auto &c = counts();
+      const OpCounts &c = counts();
+      std::lock_guard<std::mutex> lock(sum);
+      total.add += c.add; total.mul += c.mul; total.div += c.div; total.sqrt += c.sqrt;
+      total.sin += c.sin; total.cos += c.cos; total.tan += c.tan; total.atan2 += c.atan2;
+      total.hypot += c.hypot; total.rem += c.rem;
+      iters += mine;
+    };
+    const int workers = std::max(1, std::min(n, threads));
+    std::vector<std::thread> pool;
+    for (int w = 1; w < workers; ++w) pool.emplace_back(work, w, workers);
+    work(0, workers);
+    for (auto &t : pool) t.join();
+    const OpCounts &c = total;
     uint64_t v[12] = {c.add, c.mul, c.div, c.sqrt, c.sin, c.cos, c.tan, c.atan2, c.hypot, c.rem,
                       iters, uint64_t(steps) * n * substeps};
     std::memcpy(out, v, sizeof(v));

@@ -12,12 +12,14 @@
 # CMake/pybind11 build of this module segfaulted in its constructor when numpy
 # was imported first, the direct build does not.  Flags follow the reference's
 # CMakeLists.txt (-O3, -ffp-contract=off).
+#
+# DUCK_REFERENCE names the reference checkout; without it nothing is built.
 set -euo pipefail
-REF=${DUCK_REFERENCE:-/root/reference}
+REF=${DUCK_REFERENCE:-}
 HERE=$(cd "$(dirname "$0")" && pwd)
 OUT="$HERE/_ref"
-if [ ! -f "$REF/src/cuda/kernel.cuh" ]; then
-  echo "reference sources not found under $REF; skipping oracle/_ref" >&2
+if [ -z "$REF" ] || [ ! -f "$REF/src/cuda/kernel.cuh" ]; then
+  echo "reference sources not found (DUCK_REFERENCE='$REF'); skipping oracle/_ref" >&2
   exit 0
 fi
 mkdir -p "$OUT"

@@ -54,7 +54,7 @@ def library():
             fn = getattr(lib, "avbd_oracle_" + name)
             fn.argtypes = args
             fn.restype = I
-        lib.avbd_oracle_count_ops.argtypes = [ctypes.c_char_p, I, D, I, P, P, P, I, I, D, D, P]
+        lib.avbd_oracle_count_ops.argtypes = [ctypes.c_char_p, I, D, I, P, P, P, P, I, I, D, D, I, P]
         lib.avbd_oracle_count_ops.restype = I
         _lib = lib
     return _lib
@@ -167,17 +167,24 @@ class OracleBatch:
         _check(library().avbd_oracle_import(self._h, int(env), _ptr(record)))
 
 
-def count_ops(model, home, targets, forces, dt, iterations, substeps, kp, limit):
+def count_ops(model, home, targets, forces, dt, iterations, substeps, kp, limit, records=None, threads=1):
     """Count fp32 solver operations of ``targets.shape[0]`` control steps on
-    ``targets.shape[1]`` envs.  Returns a dict of counts."""
+    ``targets.shape[1]`` envs, started from ``records`` (float32 portable
+    records [n, record length], e.g. exported from a GPU batch) or else from
+    HOME, on ``threads`` host threads.  Returns a dict of counts."""
     targets = np.ascontiguousarray(targets, np.float32)
     steps, n, _ = targets.shape
     home = np.ascontiguousarray(home, np.float32)
     forces = np.ascontiguousarray(forces, np.float32)
+    if records is not None:
+        records = np.ascontiguousarray(records, np.float32)
+        if records.ndim != 2 or records.shape[0] != n:
+            raise ValueError(f"records must be [{n}, record length], got {records.shape}")
     out = np.zeros(12, np.uint64)
     _check(library().avbd_oracle_count_ops(str(model).encode(), n, float(dt), int(iterations),
-                                           _ptr(home), _ptr(targets), _ptr(forces), steps,
-                                           int(substeps), float(kp), float(limit), _ptr(out)))
+                                           _ptr(home), None if records is None else _ptr(records),
+                                           _ptr(targets), _ptr(forces), steps,
+                                           int(substeps), float(kp), float(limit), int(threads), _ptr(out)))
     names = ("add", "mul", "div", "sqrt", "sin", "cos", "tan", "atan2", "hypot", "remainder",
              "gs_iterations", "physics_steps")
     return dict(zip(names, (int(v) for v in out)))

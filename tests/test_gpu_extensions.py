@@ -1,11 +1,11 @@
 """GPU: the two declared extensions beyond the reference's envelope, checked
 against the CPU oracle restating the same algorithm.
 
-* More than 32 body-collision pairs (all 91 non-adjacent
-  pairs of the 15-link biped).  The reference loader rejects more than 32
+* More than 32 body-collision pairs (all 91 non-adjacent pairs of the
+  15-link biped).  The reference loader rejects more than 32
   pairs (solver.cpp:151-152); ``max_pairs`` raises the limit in both this
   library and the oracle.  Contact sets stay bit-exact, poses within 1e-4.
-* Per-environment physical parameters (domain randomisation, config 5).  The
+* Per-environment physical parameters (domain randomisation).  The
   reference shares one model across all envs (kernel.cuh:331); here a batch
   with per-env masses, inertias and ground frictions must match, env by env,
   oracle batches built from model files carrying each env's values.

@@ -153,3 +153,24 @@ def test_operation_count(biped_model, biped_meta):
     per_step = (c["add"] + c["mul"] + c["div"] + c["sqrt"]) / c["physics_steps"]
     assert 1e5 < per_step < 1e7
     assert c["gs_iterations"] <= c["physics_steps"] * 10
+
+
+def test_operation_count_from_records(biped_model, biped_meta):
+    """Counting from exported records continues the HOME run exactly: the
+    counts of 3 + 2 steps equal those of 5 steps (the record round trip and
+    the counting scalar both reproduce the solver's state bit for bit)."""
+    n = 3
+    home = np.asarray(biped_meta["home"], np.float32)
+    targets = helpers.targets(biped_meta, 5, n, 0.1, seed=4)
+    forces = np.zeros((n, 3), np.float32)
+    args = (0.005, 10, 4, 20.0, 2.0)
+    whole = count_ops(biped_model, home, targets, forces, *args)
+    first = count_ops(biped_model, home, targets[:3], forces, *args)
+    ora = OracleBatch(biped_model, n, 0.005, 10)
+    ora.reset(np.ones(n, bool), np.tile(home, (n, 1)), np.zeros((n, 6), np.float32))
+    for s in range(3):
+        ora.step(targets[s], forces, 4, 20.0, 2.0)
+    records = np.stack([ora.export_env(e) for e in range(n)])
+    rest = count_ops(biped_model, home, targets[3:], forces, *args, records=records)
+    for key in whole:
+        assert whole[key] == first[key] + rest[key], key

@@ -1,14 +1,16 @@
 """GPU test of duck_batch_reference_static, the allocation-free entry point.
 
 Some callers cannot call cudaMalloc when they want a single-environment check
-of the solver: code running under CUDA graph stream capture, code under a
-memory pool that forbids raw device allocation, and control loops that cannot
-take the device-wide synchronisation of cudaMalloc/cudaFree.  For them the
-library keeps this entry point's scratch in a fixed 32 KiB device array
-instead of allocating it.  The test calls it through the C ABI and checks its
-outputs against duck_batch_reference (which allocates its scratch) on two
-calls in a row, then checks that a model too large for the fixed array is
-rejected with a clear error.  It lives in a file of its own that pytest
+of the solver: a host framework whose caching allocator owns the device memory
+and forbids raw allocation beside it, a process held to a fixed device-memory
+budget, and real-time control loops that must not take the implicit
+synchronisation of cudaMalloc/cudaFree.  For them the library keeps this entry
+point's scratch in a fixed 32 KiB device array instead of allocating it.  The
+test calls it through the C ABI and checks its outputs against
+duck_batch_reference (which allocates its scratch) on two calls in a row, on a
+batch with per-environment masses, inertias and frictions installed, then
+checks that a model too large for the fixed array is rejected with a clear
+error.  It lives in a file of its own that pytest
 collects last, and passes alone in a fresh process as well as after the rest
 of the suite.
 """
@@ -69,6 +71,37 @@ def test_static_reference_matches_allocating_reference(biped_model, biped_meta, 
             assert np.isfinite(a).all()
             np.testing.assert_allclose(a, b, rtol=0, atol=POSE_TOL)
         assert out[2][5] == 0 and out[2][2] == ref[2][2]
+
+
+def test_static_reference_uses_per_env_parameters(biped_model, biped_meta):
+    """With per-environment parameters installed both entry points run
+    environment 0's values, and those values change the result."""
+    from duck_gym_b200 import CudaBatch
+
+    lib = bind()
+    batch = CudaBatch(biped_model, 4, 0.005, 10)
+    home = np.asarray(biped_meta["home"])
+    rng = np.random.default_rng(32)
+    target, forces = home + rng.normal(0, 0.05, home.size), np.zeros(3)
+    _, plain = call(lib, "duck_batch_reference", batch, target, forces, 8, 20.0, 2.0)
+    nb, ns = batch.num_bodies, batch.num_shapes
+    lines = [line for line in open(biped_model).read().splitlines() if line.strip()]
+    mass0 = np.array([float(lines[2 + b].split()[1]) for b in range(nb)], np.float32)
+    inertia0 = np.array([[float(v) for v in lines[2 + b].split()[2:5]] for b in range(nb)], np.float32)
+    scale = rng.uniform(1.3, 1.6, (4, nb)).astype(np.float32)
+    dev = lambda a: torch.as_tensor(a, device="cuda").contiguous()
+    batch.set_parameters(dev(mass0[None] * scale), dev(inertia0[None] * scale[..., None]),
+                         dev(np.full((4, ns), 0.4, np.float32)))
+    for _ in range(2):
+        before = batch.launches
+        s1, ref = call(lib, "duck_batch_reference", batch, target, forces, 8, 20.0, 2.0)
+        middle = batch.launches
+        s2, out = call(lib, "duck_batch_reference_static", batch, target, forces, 8, 20.0, 2.0)
+        assert s1 == 0 and s2 == 0, lib.duck_last_error()
+        assert batch.launches - middle == middle - before  # both count their launches
+        for a, b in zip(out, ref):
+            np.testing.assert_allclose(a, b, rtol=0, atol=POSE_TOL)
+    assert np.abs(ref[0] - plain[0]).max() > 10 * POSE_TOL  # the parameters took effect
 
 
 def chain_model(links=31):
