@@ -60,3 +60,104 @@ def home_q(meta, envs, noise=0.0, seed=1):
     rng = np.random.default_rng(seed)
     home = np.asarray(meta["home"], np.float32)
     return (home + rng.normal(0, noise, (envs, home.size))).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# One-ulp sensitivity of the reference algorithm (the velocity envelope).
+#
+# Velocities are (x - x0) / h, so at dt = 5 ms they magnify fp32 rounding of
+# the poses 200 times, and a stick/slip, limit or friction switch taken the
+# other way moves them by much more.  The envelope the GPU is held to is
+# measured, not chosen: on every teacher-forced check the CPU oracle (bit for
+# bit the reference's own CpuBatch32) also advances copies of the same state
+# whose body poses and velocities were moved by one ulp, and the spread of
+# those copies around the unperturbed oracle is the reference algorithm's own
+# sensitivity to one rounding of its input.
+
+def body_slots(record_length, nb, fp_dtype):
+    """Indices of the body pose/velocity words (x, q, v, w) of bodies 1..B-1
+    in a portable record (header 8, then 16 words per body)."""
+    idx = [8 + 16 * b + k for b in range(1, nb) for k in range(13)]
+    return np.asarray(idx, np.int64)
+
+
+def perturb_records(records, nb, seed):
+    """Copies of `records` [n, L] with every body pose/velocity word moved by
+    one ulp, up or down at random (seeded)."""
+    out = np.array(records, copy=True)
+    idx = body_slots(out.shape[1], nb, out.dtype)
+    rng = np.random.default_rng(seed)
+    up = rng.random((out.shape[0], idx.size)) < 0.5
+    vals = out[:, idx]
+    out[:, idx] = np.where(up, np.nextafter(vals, np.inf, dtype=out.dtype),
+                           np.nextafter(vals, -np.inf, dtype=out.dtype))
+    return out
+
+
+class UlpTwins:
+    """Oracle copies advanced from one-ulp-perturbed copies of a state."""
+
+    def __init__(self, make_oracle, seeds=(101, 202, 303)):
+        self.seeds = seeds
+        self.twins = [make_oracle() for _ in seeds]
+
+    def advance(self, records, step):
+        """Load perturbed copies of `records`, apply `step(batch)` to each
+        twin, return their states."""
+        states = []
+        for seed, twin in zip(self.seeds, self.twins):
+            rec = perturb_records(records, twin.num_bodies, seed)
+            for e in range(twin.num_envs):
+                twin.import_env(e, rec[e])
+            step(twin)
+            states.append(twin.state())
+        return states
+
+
+class VelocityStats:
+    """Pools |velocity differences| over all checks of one test, for the GPU
+    and for the one-ulp twins, and holds the GPU to the twins' envelope:
+
+    * the fraction of components beyond `tol` may be at most twice the twins'
+      (or 0.1 %, whichever is larger);
+    * the largest deviation may be at most twice the twins' largest (or `tol`).
+    """
+
+    def __init__(self, tol):
+        self.tol, self.gpu, self.ulp = tol, {}, {}
+
+    def add(self, what, actual, expected, twins=()):
+        self.gpu.setdefault(what, []).append(np.abs(actual - expected).ravel())
+        for t in twins:
+            self.ulp.setdefault(what, []).append(np.abs(t - expected).ravel())
+
+    def envelope(self, what):
+        diff = np.concatenate(self.ulp[what])
+        return float(np.mean(diff > self.tol)), float(diff.max())
+
+    def check(self):
+        for what, parts in self.gpu.items():
+            diff = np.concatenate(parts)
+            if diff.size == 0:
+                continue
+            outside, worst = float(np.mean(diff > self.tol)), float(diff.max())
+            ulp_outside, ulp_worst = self.envelope(what) if what in self.ulp else (0.0, 0.0)
+            print(f"{what}: GPU {outside:.5f} beyond {self.tol} (max {worst:.3e}); one-ulp twins "
+                  f"{ulp_outside:.5f} (max {ulp_worst:.3e}); {diff.size} components")
+            assert outside <= max(2 * ulp_outside, 1e-3), \
+                f"{what}: {outside:.5f} of components beyond {self.tol}, twins {ulp_outside:.5f}"
+            assert worst <= max(self.tol, 2 * ulp_worst), \
+                f"{what}: max deviation {worst:.3e}, twins {ulp_worst:.3e}"
+
+
+def contact_keys_from_records(records, nb, nj):
+    """Per-env (body, shape, feature, other, otherShape) rows read from
+    portable records [n, L]: header word 1 is the contact count, contacts
+    start after the bodies (16 words each) and joints (22 words each)."""
+    base = 8 + 16 * nb + 22 * nj
+    out = []
+    for rec in np.asarray(records):
+        count = int(rec[1])
+        rows = rec[base:base + 32 * count].reshape(count, 32)[:, :5]
+        out.append(rows.astype(np.int64))
+    return out

@@ -18,7 +18,7 @@ import pytest
 import torch
 
 import helpers
-from test_gpu_parity import VelocityStats, compare_substep, dev, load_oracle_state
+from test_gpu_parity import VelocityStats, dev, teacher_check
 
 pytestmark = pytest.mark.gpu
 
@@ -68,14 +68,13 @@ def test_91_pair_self_contact_teacher_forced(pair_biped):
     forces = np.zeros((n, 3), np.float32)
     ora.reset(np.ones(n, bool), helpers.home_q(meta, n, noise=0.02), np.zeros((n, 6), np.float32))
     stats = VelocityStats()
+    twins = helpers.UlpTwins(lambda: oracle(path, n, max_pairs=128))
     checked = self_seen = 0
     for s in range(steps):
         for sub in range(4):
             if (4 * s + sub) % 3 == 0:
-                load_oracle_state(gpu, ora)
-                gpu.step(dev(t[s]), dev(forces), 1, kp, limit)
-                ora.step(t[s], forces, 1, kp, limit)
-                compare_substep(gpu, ora, stats)
+                teacher_check(gpu, ora, twins, lambda: gpu.step(dev(t[s]), dev(forces), 1, kp, limit),
+                              lambda b: b.step(t[s], forces, 1, kp, limit), stats)
                 np.testing.assert_array_equal(gpu.contact_counts().cpu().numpy(), ora.contact_counts())
                 checked += 1
             else:
@@ -119,11 +118,14 @@ def test_domain_randomization_matches_per_env_models(tmp_path, biped_model, bipe
     for e, o in enumerate(oras):
         o.reset(np.ones(1, bool), helpers.home_q(biped_meta, 1, noise=0.02, seed=e), np.zeros((1, 6), np.float32))
     offset = np.zeros((n, 3), np.float32)
-    worst = 0.0
+    stats = VelocityStats()
+    twins = [helpers.UlpTwins(lambda e=e: oracle(tmp_path / f"env{e}.duck", 1)) for e in range(n)]
     for s in range(steps):
         rec = np.concatenate([o.export_env(0)[None] for o in oras])
         gpu.import_records(dev(rec))
         gpu.step(dev(t[s]), dev(pushes[s]), 1, kp, limit)
+        twin_states = [tw.advance(rec[e:e + 1], lambda b, e=e: b.step(t[s][e:e + 1], pushes[s][e:e + 1], 1, kp,
+                                                                       limit)) for e, tw in enumerate(twins)]
         for e, o in enumerate(oras):
             o.step(t[s][e:e + 1], pushes[s][e:e + 1], 1, kp, limit)
         gb, gj, gd = [x.cpu().numpy() for x in gpu.state()]
@@ -133,11 +135,12 @@ def test_domain_randomization_matches_per_env_models(tmp_path, biped_model, bipe
             np.testing.assert_array_equal(gpu.contact_keys(e), o.contact_keys(0), err_msg=f"env {e} step {s}")
             np.testing.assert_allclose(gb[e, :, :7], ob[0, :, :7], rtol=0, atol=1e-4)
             np.testing.assert_allclose(gj[e, :, 0], oj[0, :, 0], rtol=0, atol=1e-4)
-            worst = max(worst, float(np.abs(gb[e, :, 7:] - ob[0, :, 7:]).max()))
+            stats.add("body velocity", gb[e, :, 7:], ob[0, :, 7:], [ts[0][0, :, 7:] for ts in twin_states[e]])
+            stats.add("joint rate", gj[e, :, 1], oj[0, :, 1], [ts[1][0, :, 1] for ts in twin_states[e]])
         loads = gpu.generalized_loads(dev(offset)).cpu().numpy()
         for e, o in enumerate(oras):
             np.testing.assert_allclose(loads[e], o.generalized_loads(offset[e:e + 1])[0], rtol=1e-3, atol=2e-4)
-    assert worst < 2e-2
+    stats.check()
     # The envs really differ: the same controls give different trajectories.
     assert np.abs(gb[0, 1, :3] - gb[1, 1, :3]).max() > 1e-6
 
