@@ -264,6 +264,68 @@ def cpu_baseline(model, meta, seconds=12.0, envs=1024):
                       f"({SUBSTEPS} substeps), wall clock"}
 
 
+def reference_cuda_module():
+    """The reference's own CUDA extension rebuilt for sm_100a by
+    oracle/build_ref_cuda.py, or None."""
+    import importlib.util
+
+    path = ROOT / "oracle" / "_ref" / "cuda" / "_duck_cuda.so"
+    if not path.exists():
+        return None
+    import torch  # noqa: F401  (the extension links libtorch)
+
+    spec = importlib.util.spec_from_file_location("_duck_cuda", path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def reference_cuda(model, meta, envs, device, steps=40, trials=5):
+    """Context number: the reference's own CUDA step (extension.cu advance,
+    one 32-thread block per env) rebuilt for sm_100a and run on this GPU on
+    the same workload -- settled 200 steps, then `trials` x `steps` control
+    steps timed with CUDA events, L2 flushed between steps, median trial.
+    Both of its compact-state variants are timed (state in global memory, and
+    the whole state copied to shared memory)."""
+    import torch
+
+    ext = reference_cuda_module()
+    if ext is None:
+        return None
+    kp, limit = meta["kp"], meta["torque_limit"]
+    target = torch.from_numpy(fixed_targets(meta, envs, 0)).to(device)
+    forces = torch.zeros(envs, 3, device=device)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+    out = {}
+    for shared in (False, True):
+        sim = ext.CudaBatch(str(model), envs, DT, ITERATIONS, device.index, False, True, shared)
+        for _ in range(SETTLE):
+            sim.step(target, forces, SUBSTEPS, kp, limit)
+        values = []
+        for _ in range(trials):
+            total = 0.0
+            for _ in range(steps):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                sim.step(target, forces, SUBSTEPS, kp, limit)
+                b.record(stream)
+                b.synchronize()
+                total += a.elapsed_time(b) / 1e3
+            values.append(envs * SUBSTEPS * steps / total)
+        failed = float((sim.state()[2][:, 5] > 0).float().mean())
+        out["shared_memory" if shared else "global_memory"] = {"value": statistics.median(values),
+                                                               "failed_env_fraction": failed}
+        del sim
+    best = max(out.values(), key=lambda v: v["value"])["value"]
+    return {"value": best, "unit": UNIT, "variants": out,
+            "kernel": "reference extension.cu advance<S,Shared> (specialized compact state), built for sm_100a "
+                      "with the reference's flags by oracle/build_ref_cuda.py",
+            "sample": f"{envs} envs after {SETTLE} settle steps, median of {trials} trials x {steps} control steps, "
+                      "CUDA events, L2 flushed between steps"}
+
+
 def traffic_from_profile():
     """DRAM bytes per advance launch from the committed ncu summary, if any."""
     path = ROOT / "profiles" / "advance_biped4096.txt"
@@ -694,6 +756,10 @@ def main():
             }
             if not args.no_cpu_baseline and world == 1:
                 line["cpu_baseline"] = cpu_baseline(model, meta)
+                ref_gpu = reference_cuda(model, meta, envs, device)
+                if ref_gpu is not None:
+                    ref_gpu["ours_over_reference"] = value / ref_gpu["value"]
+                    line["reference_cuda"] = ref_gpu
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()

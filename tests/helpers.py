@@ -115,39 +115,44 @@ class UlpTwins:
 
 
 class VelocityStats:
-    """Pools |velocity differences| over all checks of one test, for the GPU
-    and for the one-ulp twins, and holds the GPU to the twins' envelope:
+    """Pools |differences| of one quantity over all checks of one test, for
+    the GPU and for the one-ulp twins, and holds the GPU's distribution of
+    deviations to the twins' at every level t = tol, 10 tol, 100 tol, ...:
 
-    * the fraction of components beyond `tol` may be at most twice the twins'
-      (or 0.1 %, whichever is larger);
-    * the largest deviation may be at most twice the twins' largest (or `tol`).
+        fraction of GPU components beyond t
+            <= 2 x the twins' fraction beyond t (+ `floor` at t = tol)
+               + 3 components (sampling noise of the tail).
+
+    With floor = 0 and twins that stay within `tol` this is the plain bound
+    `tol` with at most three outliers.
     """
 
-    def __init__(self, tol):
-        self.tol, self.gpu, self.ulp = tol, {}, {}
+    def __init__(self, tol, floor=1e-3):
+        self.tol, self.floor, self.gpu, self.ulp = tol, floor, {}, {}
 
     def add(self, what, actual, expected, twins=()):
         self.gpu.setdefault(what, []).append(np.abs(actual - expected).ravel())
         for t in twins:
             self.ulp.setdefault(what, []).append(np.abs(t - expected).ravel())
 
-    def envelope(self, what):
-        diff = np.concatenate(self.ulp[what])
-        return float(np.mean(diff > self.tol)), float(diff.max())
-
     def check(self):
         for what, parts in self.gpu.items():
             diff = np.concatenate(parts)
             if diff.size == 0:
                 continue
-            outside, worst = float(np.mean(diff > self.tol)), float(diff.max())
-            ulp_outside, ulp_worst = self.envelope(what) if what in self.ulp else (0.0, 0.0)
-            print(f"{what}: GPU {outside:.5f} beyond {self.tol} (max {worst:.3e}); one-ulp twins "
-                  f"{ulp_outside:.5f} (max {ulp_worst:.3e}); {diff.size} components")
-            assert outside <= max(2 * ulp_outside, 1e-3), \
-                f"{what}: {outside:.5f} of components beyond {self.tol}, twins {ulp_outside:.5f}"
-            assert worst <= max(self.tol, 2 * ulp_worst), \
-                f"{what}: max deviation {worst:.3e}, twins {ulp_worst:.3e}"
+            ulp = np.concatenate(self.ulp[what]) if what in self.ulp else np.zeros(1)
+            print(f"{what}: GPU {np.mean(diff > self.tol):.6f} beyond {self.tol} (max {diff.max():.3e}); "
+                  f"one-ulp twins {np.mean(ulp > self.tol):.6f} (max {ulp.max():.3e}); {diff.size} components")
+            level = self.tol
+            while True:
+                gpu = float(np.mean(diff > level))
+                allowed = 2 * float(np.mean(ulp > level)) + (self.floor if level == self.tol else 0.0) \
+                    + 3.0 / diff.size
+                assert gpu <= allowed, (f"{what}: {gpu:.6f} of components beyond {level:.1e}, "
+                                        f"allowed {allowed:.6f} from the one-ulp twins")
+                if level >= diff.max():
+                    break
+                level *= 10
 
 
 def contact_keys_from_records(records, nb, nj):

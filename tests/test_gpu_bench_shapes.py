@@ -11,8 +11,10 @@ times.
   N(0, 0.1 rad) targets drawn per joint per step, ensemble statistics (mean
   base height, joint RMS, contact count) within 1 % of the oracle's.
 
-Contact sets and failure flags bit exact, poses within 1e-4, velocities held
-to the one-ulp envelope measured on the same states (helpers.VelocityStats).
+Contact sets and failure flags bit exact; poses within 1e-4 and velocities
+within 1e-3, each up to the one-ulp envelope of the reference algorithm
+measured on the same states (helpers.VelocityStats; with no outlier among
+the twins the pose bound is the plain 1e-4).
 """
 
 import json
@@ -49,9 +51,10 @@ def load(ora, records):
         ora.import_env(e, records[e])
 
 
-def compare_records(gpu, ora, stats, twin_states=(), pose_tol=POSE_TOL):
-    """Contact sets from the records (one bulk copy), failure flags, poses,
-    joint angles and counts exactly or within tolerance; velocities pooled."""
+def compare_records(gpu, ora, stats, poses, twin_states=()):
+    """Contact sets from the records (one bulk copy), failure flags and
+    contact counts exactly; poses and joint angles (`poses`) and velocities
+    (`stats`) pooled against the one-ulp twins on the same states."""
     nb, nj = gpu.num_bodies, gpu.num_joints
     grec = gpu.export_records().cpu().numpy()
     orec = np.stack([ora.export_env(e) for e in range(ora.num_envs)])
@@ -63,9 +66,12 @@ def compare_records(gpu, ora, stats, twin_states=(), pose_tol=POSE_TOL):
     ob, oj, od = ora.state()
     np.testing.assert_array_equal(gd[:, 5], od[:, 5], err_msg="failure flags differ")
     live = od[:, 5] == 0
-    np.testing.assert_allclose(gb[live][..., :7], ob[live][..., :7], rtol=0, atol=pose_tol)
-    np.testing.assert_allclose(gj[live][..., 0], oj[live][..., 0], rtol=0, atol=pose_tol)
     np.testing.assert_array_equal(gd[live][:, 2], od[live][:, 2])
+    far = np.abs(gb[..., :7] - ob[..., :7]).max(axis=(1, 2))
+    worst = int(np.argmax(np.where(live, far, 0)))
+    print(f"largest pose deviation {far[worst]:.3e} in env {worst}")
+    poses.add("body pose", gb[live][..., :7], ob[live][..., :7], [t[0][live][..., :7] for t in twin_states])
+    poses.add("joint angle", gj[live][..., 0], oj[live][..., 0], [t[1][live][..., 0] for t in twin_states])
     stats.add("body velocity", gb[live][..., 7:], ob[live][..., 7:], [t[0][live][..., 7:] for t in twin_states])
     stats.add("joint rate", gj[live][..., 1], oj[live][..., 1], [t[1][live][..., 1] for t in twin_states])
     return int(live.sum())
@@ -86,7 +92,7 @@ def test_bench_shape_4096_envs_from_settled_state(biped_model, biped_meta):
     ora = oracle(biped_model, envs)
     twins = helpers.UlpTwins(lambda: oracle(biped_model, envs))
     forces = np.zeros((envs, 3), np.float32)
-    stats = VelocityStats()
+    stats, poses = VelocityStats(), helpers.VelocityStats(POSE_TOL, floor=0.0)
     # Two substeps teacher-forced from the settled state, then a full call.
     load(ora, settled)
     for _ in range(2):
@@ -95,8 +101,9 @@ def test_bench_shape_4096_envs_from_settled_state(biped_model, biped_meta):
         gpu.step(tg, fg, 1, kp, limit)
         states = twins.advance(rec, lambda b: b.step(target, forces, 1, kp, limit))
         ora.step(target, forces, 1, kp, limit)
-        live = compare_records(gpu, ora, stats, states)
+        live = compare_records(gpu, ora, stats, poses, states)
     stats.check()
+    poses.check()
     assert live >= 0.5 * envs and ora.state()[2][:, 2].mean() > 2   # standing, on its feet
     load(ora, settled)
     gpu.import_records(dev(settled))
@@ -125,9 +132,9 @@ def test_self_contact_16384_envs(tmp_path):
         gpu.step(dev(t[s]), fg, 4, kp, limit)
     start = gpu.export_records().cpu().numpy()
     ora = oracle(path, envs, max_pairs=128)
-    twins = helpers.UlpTwins(lambda: oracle(path, envs, max_pairs=128), seeds=(101,))
+    twins = helpers.UlpTwins(lambda: oracle(path, envs, max_pairs=128))
     forces = np.zeros((envs, 3), np.float32)
-    stats = VelocityStats()
+    stats, poses = VelocityStats(), helpers.VelocityStats(POSE_TOL, floor=0.0)
     load(ora, start)
     target = t[-1]
     self_contacts = 0
@@ -137,10 +144,11 @@ def test_self_contact_16384_envs(tmp_path):
         gpu.step(dev(target), fg, 1, kp, limit)
         states = twins.advance(rec, lambda b: b.step(target, forces, 1, kp, limit))
         ora.step(target, forces, 1, kp, limit)
-        compare_records(gpu, ora, stats, states)
+        compare_records(gpu, ora, stats, poses, states)
         np.testing.assert_array_equal(gpu.contact_counts().cpu().numpy(), ora.contact_counts())
         self_contacts += int(ora.contact_counts()[:, 1].sum())
     stats.check()
+    poses.check()
     assert self_contacts > 100
 
 
