@@ -330,12 +330,25 @@ template <class R, int T, bool P = true> struct Solver {
     V3<R> vv = xadd(v, xcross(w, xsub(wp, x)));
     return rmin(wp.z, xadd(xadd(wp.z, xmul(dt, vv.z)), xmul(dt2, accel)));
   }
+  // The reference's lateral test hypot(dx, dy) < .005 (kernel.cuh:355):
+  // its float hypot is correctly rounded and the comparison is in double.
+  // The root and both roundings are monotone in s = dx^2 + dy^2 (exact
+  // squares, summed in double), so the test is s < kPickApart2, the least
+  // double whose rounded root narrows to a float >= .005.  The constant is
+  // found by bisection over the doubles (tests/test_pick_threshold.py derives
+  // it again); this replaces a double square root per test.
+  static constexpr double kPickApart2 = 0x1.a36e30068db92p-16;
+  static __device__ __forceinline__ bool pickClose(float dx, float dy) {
+    const double x = dx, y = dy;
+    return __dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)) < kPickApart2;
+  }
+  static __device__ __forceinline__ bool pickClose(double dx, double dy) { return xhypot(dx, dy) < .005; }
   // A candidate pick must lie 5 mm or more (laterally) from the earlier ones.
   static __device__ __forceinline__ bool pickApart(V3<R> wp, const V3<R> *world, int n) {
     bool ok = true;
 #pragma unroll
     for (int c = 0; c < 3; ++c)
-      if (c < n && double(xhypot(xsub(world[c].x, wp.x), xsub(world[c].y, wp.y))) < .005) ok = false;
+      if (c < n && pickClose(xsub(world[c].x, wp.x), xsub(world[c].y, wp.y))) ok = false;
     return ok;
   }
   // Up to four lowest, laterally separated support points of shape s that are
@@ -394,8 +407,7 @@ template <class R, int T, bool P = true> struct Solver {
         ++n;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          if ((open >> k & 1u) &&
-              double(xhypot(xsub(bestWorld.x, wps[k].x), xsub(bestWorld.y, wps[k].y))) < .005)
+          if ((open >> k & 1u) && pickClose(xsub(bestWorld.x, wps[k].x), xsub(bestWorld.y, wps[k].y)))
             open &= ~(1u << k);
       }
       return n;
