@@ -740,15 +740,30 @@ template <class R, int T, bool P = true> struct Solver {
   }
 
   // ------------------------------------------------------------ primal
+  // A hinge's multipliers and penalties (7 rows) and its dry-friction pair,
+  // read once from shared memory and handed to the stamp or the dual update
+  // in registers.
+  struct Multipliers {
+    R lam[7], pen[7], lf, pf;
+  };
+  __device__ __forceinline__ void loadMultipliers(int j, Multipliers &mu) const {
+    const SV lam = S + (L.JL + 7 * j), pen = S + (L.JP + 7 * j);
+#pragma unroll
+    for (int k = 0; k < 7; ++k) { mu.lam[k] = lam[k]; mu.pen[k] = pen[k]; }
+    mu.lf = S[L.JLF + j];
+    mu.pf = S[L.JPF + j];
+  }
   // Rows of hinge j acting on body bi (kernel.cuh:863-913): anchor rows with
   // their geometric stiffness, axis-orthogonality rows, then limits, PD drive,
   // damping/armature and dry friction summed along the hinge axis.
-  __device__ __forceinline__ void stampHinge(int bi, int j, const JointGeo &e, R *H, R *g, R kp, R limit) const {
+  __device__ __forceinline__ void stampHinge(int bi, int j, const JointGeo &e, const Multipliers &mu, R *H, R *g, R kp,
+                                             R limit) const {
     const R h = m->dt, alpha = m->alpha;
     const R ih = R(1) / h, ih2 = ih * ih;
     const bool parent = e.a == bi;
     const R s = parent ? R(1) : R(-1);
-    const SV lam = S + (L.JL + 7 * j), pen = S + (L.JP + 7 * j), c0 = S + (L.JC0 + 7 * j);
+    const R *lam = mu.lam, *pen = mu.pen;
+    const SV c0 = S + (L.JC0 + 7 * j);
     const V3<R> r = parent ? e.ra : e.rb;
     R f3[3];
 #pragma unroll
@@ -795,9 +810,9 @@ template <class R, int T, bool P = true> struct Solver {
     }
     const R fl = S[L.JFL + j];
     if (fl > R(0)) {
-      R trial = S[L.JLF + j] + S[L.JPF + j] * delta;
+      R trial = mu.lf + mu.pf * delta;
       force += rclamp(trial, -fl, fl);
-      if (fabs(trial) < fl) stiff += S[L.JPF + j];
+      if (fabs(trial) < fl) stiff += mu.pf;
     }
     stampAngular(H, g, e.axis * (-s), force, stiff);
   }
@@ -909,7 +924,9 @@ template <class R, int T, bool P = true> struct Solver {
       const int j = ldg(m->csrJoint[adj]);
       JointGeo e;
       evalJoint(j, e);
-      stampHinge(bi, j, e, H, g, kp, limit);
+      Multipliers mu;
+      loadMultipliers(j, mu);
+      stampHinge(bi, j, e, mu, H, g, kp, limit);
     }
     // Contacts touching bi, in list order.
     const int nGround = I[iGround];
@@ -968,7 +985,7 @@ template <class R, int T, bool P = true> struct Solver {
 
   // Dual update of hinge j (kernel.cuh:991-1028): multipliers, penalty ramps,
   // dry friction; folds the constraint error into *error.
-  __device__ __forceinline__ void dualHinge(int j, const JointGeo &e, R &error) const {
+  __device__ __forceinline__ void dualHinge(int j, const JointGeo &e, R &error, Multipliers &mu) const {
     const R alpha = m->alpha;
     const SV lam = S + (L.JL + 7 * j), pen = S + (L.JP + 7 * j), c0 = S + (L.JC0 + 7 * j);
     const int rows = e.limited ? 7 : 5;
@@ -976,19 +993,24 @@ template <class R, int T, bool P = true> struct Solver {
     for (int k = 0; k < 7; ++k) {
       if (k >= rows) break;
       R c = e.C[k] - alpha * (k < 5 ? c0[k] : rmin(c0[k], R(0)));
-      R f = lam[k] + pen[k] * c;
-      lam[k] = k >= 5 ? rmin(f, R(0)) : f;
-      if (k < 5 || f < R(0))
-        pen[k] = rmin(pen[k] + (k < 3 ? m->betaLinear : m->betaAngular) * fabs(c), k < 3 ? R(1e9) : R(1e7));
+      R f = mu.lam[k] + mu.pen[k] * c;
+      mu.lam[k] = k >= 5 ? rmin(f, R(0)) : f;
+      lam[k] = mu.lam[k];
+      if (k < 5 || f < R(0)) {
+        mu.pen[k] = rmin(mu.pen[k] + (k < 3 ? m->betaLinear : m->betaAngular) * fabs(c), k < 3 ? R(1e9) : R(1e7));
+        pen[k] = mu.pen[k];
+      }
       error = rmax(error, k < 5 ? R(fabs(c)) : rmax(R(0), -c));
     }
     const R fl = S[L.JFL + j];
     if (fl > R(0)) {
       R delta = wrapAngle(e.angle - S[L.JA0 + j]);
-      R trial = S[L.JLF + j] + S[L.JPF + j] * delta;
+      R trial = mu.lf + mu.pf * delta;
       R lf = rclamp(trial, -fl, fl);
-      R pf = S[L.JPF + j];
+      R pf = mu.pf;
       if (fabs(trial) < fl) pf = rmin(pf + m->betaAngular * R(fabs(delta)), R(1e7));
+      mu.lf = lf;
+      mu.pf = pf;
       S[L.JLF + j] = lf;
       S[L.JPF + j] = pf;
       R residual = lf + pf * delta;
@@ -1170,7 +1192,9 @@ template <class R, int T, bool P = true> struct Solver {
       for (int j = team.lane; j < nj; j += T) {
         JointGeo e;
         evalJoint(j, e);
-        dualHinge(j, e, error);
+        Multipliers mu;
+        loadMultipliers(j, mu);
+        dualHinge(j, e, error, mu);
       }
       // Contact multipliers, stick flags and penalties (kernel.cuh:1029-1052).
       const int n = I[iCount], nGround = I[iGround];
