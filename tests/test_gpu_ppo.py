@@ -76,3 +76,56 @@ def test_graphed_update_matches_eager(tmp_path):
     assert agent.learning_rate == pytest.approx(eager_lr, rel=1e-12)
     for k in eager_stats:
         assert graphed_stats[k] == pytest.approx(eager_stats[k], rel=1e-4, abs=1e-6)
+
+
+def test_gpu_update_matches_restatement(tmp_path):
+    """One GPU rollout and one graphed minibatch step checked against the
+    numpy restatement of the published algorithm (oracle/ppo_math.py) on the
+    GPU's own buffers: GAE returns and normalised advantages; the surrogate,
+    clipped value loss, entropy and KL of the minibatch at the parameters it
+    starts from; and the learning rate the adaptive KL schedule sets, against
+    the host rule."""
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+    import numpy as np
+
+    from duck_gym_b200 import biped
+    from duck_gym_b200.bam_env import BamEnv
+    from duck_gym_b200.ppo import PPO, PPOConfig, kl_schedule_host
+    from oracle import ppo_math
+
+    biped.write_bam(tmp_path, seed=0)
+    env = BamEnv(tmp_path, num_envs=256, iterations=10, auto_reset=True, reward_enabled=True, seconds=0.1)
+    agent = PPO(env, PPOConfig(steps_per_env=8), seed=0)
+    agent.rollout()
+    agent.update()          # eager: creates the optimizer state
+    agent.rollout()
+    s, cfg = agent.storage, agent.cfg
+    host = lambda t: t.detach().double().cpu().numpy()
+    # GAE on the stored rewards, done masks and values.
+    with torch.no_grad():
+        last = agent.policy.value(agent.critic_obs)
+    returns, adv = ppo_math.gae(host(s.rewards), host(s.dones), host(s.values), host(last), cfg.gamma, cfg.lam)
+    adv = (adv - adv.mean()) / (adv.std(ddof=1) + 1e-8)
+    np.testing.assert_allclose(host(s.returns), returns, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(host(s.advantages), adv, rtol=1e-4, atol=1e-5)
+    assert s.dones.sum() > 0
+    # One minibatch of the graphed update.
+    agent._prepare_flat()
+    n = s.T * s.E
+    idx = torch.randperm(n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(3))[: n // 4]
+    flat = lambda x: x.reshape(n, *x.shape[2:])[idx]
+    with torch.no_grad():
+        mu = agent.policy.mean(flat(s.obs))
+        value = agent.policy.value(flat(s.critic_obs))
+    sigma = np.broadcast_to(host(agent.policy.std), mu.shape)
+    want = ppo_math.ppo_terms(host(mu), sigma, host(value), host(flat(s.actions)), host(flat(s.log_prob)),
+                              host(flat(s.mu)), host(flat(s.sigma)), host(flat(s.values)), host(flat(s.returns)),
+                              host(flat(s.advantages)), cfg.clip)
+    lr_before = agent.learning_rate
+    agent._idx.copy_(idx)
+    agent._run_part(0)
+    got = dict(zip(agent.STATS, agent._stats.tolist()))
+    for k in agent.STATS:
+        assert got[k] == pytest.approx(want[k], rel=2e-4, abs=2e-6), k
+    assert agent.learning_rate == pytest.approx(kl_schedule_host(lr_before, got["kl"], cfg.desired_kl), rel=1e-12)
