@@ -8,6 +8,7 @@
 #include "../../include/duck_b200.h"
 #include "aux_kernels.cuh"
 #include "bam_kernels.cuh"
+#include "ppo_kernels.cuh"
 
 #include <cstdlib>
 #include <cstring>
@@ -1029,6 +1030,39 @@ int duck_batch_set_parameters(duck_batch *b, const void *mass, const void *inert
 }
 
 int64_t duck_batch_launches(const duck_batch *b) { return b ? b->launches : 0; }
+
+int duck_ppo_loss_scratch(int batch, int actions) {
+  if (batch <= 0 || actions <= 0 || actions > kPpoMaxActions) return -1;
+  return ((batch + kPpoThreads - 1) / kPpoThreads) * ppoPartials(actions);
+}
+
+int duck_ppo_loss(int batch, int actions, const float *mu, const float *std, const float *value, const float *act,
+                  const float *old_log_prob, const float *old_mu, const float *old_sigma, const float *target_value,
+                  const float *returns, const float *advantage, double clip, double value_coef,
+                  double entropy_coef, float *scratch, float *out, float *grad_mu, float *grad_std,
+                  float *grad_value, duck_stream stream) {
+  return guarded([&] {
+    require(batch > 0 && actions > 0 && actions <= kPpoMaxActions, "Invalid PPO batch or action count");
+    require(mu && std && value && act && old_log_prob && old_mu && old_sigma && target_value && returns && advantage &&
+                scratch && out && grad_mu && grad_std && grad_value,
+            "Invalid arguments");
+    require(clip >= 0 && std::isfinite(clip) && std::isfinite(value_coef) && std::isfinite(entropy_coef),
+            "Invalid PPO coefficients");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    PpoLossArgs a{batch, actions, mu, std, value, act, old_log_prob, old_mu, old_sigma, target_value, returns,
+                  advantage, float(clip), float(value_coef), float(entropy_coef), scratch, out, grad_mu,
+                  grad_std, grad_value};
+    const int blocks = (batch + kPpoThreads - 1) / kPpoThreads;
+    if (actions <= 16) {
+      ppoLossRows<16><<<blocks, kPpoThreads, 0, s>>>(a);
+      ppoLossFinish<16><<<1, kPpoThreads, 0, s>>>(a, blocks);
+    } else {
+      ppoLossRows<32><<<blocks, kPpoThreads, 0, s>>>(a);
+      ppoLossFinish<32><<<1, kPpoThreads, 0, s>>>(a, blocks);
+    }
+    check(cudaGetLastError(), "PPO loss launch");
+  });
+}
 
 int duck_fp32_peak(int device, int iterations, double *tflops, duck_stream stream) {
   return guarded([&] {

@@ -72,6 +72,8 @@ def library():
         lib.duck_batch_launches.argtypes = [P]
         lib.duck_batch_launches.restype = ctypes.c_int64
         lib.duck_fp32_peak.argtypes = [I, I, ctypes.POINTER(D), P]
+        lib.duck_ppo_loss_scratch.argtypes = [I, I]
+        lib.duck_ppo_loss.argtypes = [I, I] + [P] * 10 + [D, D, D] + [P] * 5 + [P]
         lib.duck_env_obs_dim.argtypes = [P, P]
         lib.duck_env_targets.argtypes = [P, P, D, P, P, P, P, P, P]
         lib.duck_env_reference_targets.argtypes = [P, P, P, D, P, P, P, P, P, P, P, P]
@@ -93,7 +95,8 @@ def library():
                      "duck_batch_import", "duck_batch_contact_keys", "duck_fp32_peak", "duck_env_obs_dim",
                      "duck_env_targets", "duck_env_reference_targets", "duck_env_post_step", "duck_env_observe", "duck_env_reset_buffers",
                      "duck_bam_critic_dim", "duck_bam_step", "duck_bam_begin", "duck_bam_substep", "duck_bam_finish",
-                     "duck_bam_servo", "duck_bam_reset_buffers", "duck_bam_observe"):
+                     "duck_bam_servo", "duck_bam_reset_buffers", "duck_bam_observe", "duck_ppo_loss_scratch",
+                     "duck_ppo_loss"):
             getattr(lib, name).restype = I
         _lib = lib
     return _lib

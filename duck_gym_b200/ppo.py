@@ -53,6 +53,7 @@ class PPOConfig:
     bucket_mb: float = 0.5
     graph_rollout: bool = True   # replay the rollout's policy step from a CUDA graph (GPU only)
     graph_update: bool = True    # flat-gradient minibatch step after the first update, CUDA graphs on the GPU
+    fused_loss: bool = True      # on the GPU: the loss and its gradient in one fused CUDA pass (duck_ppo_loss)
 
 
 def mlp(sizes):
@@ -120,10 +121,52 @@ def gae(rewards, dones, values, last_values, gamma, lam):
     return returns, returns - values
 
 
+class FusedPPOLoss(torch.autograd.Function):
+    """The minibatch loss of ppo_loss and its gradient with respect to the
+    policy means, std and values in one pass of the library's fused CUDA
+    kernels (duck_ppo_loss: two launches, deterministic sums) instead of the
+    torch expression's ~80 element-wise kernels and their backward.  Returns
+    the loss and the statistics (surrogate, value loss, entropy, kl)."""
+
+    @staticmethod
+    def forward(ctx, mu, std, value, actions, old_log_prob, old_mu, old_sigma, target_values, returns, advantages,
+                clip, value_coef, entropy_coef):
+        import ctypes
+
+        from .cuda_batch import _raise, _stream, library
+
+        lib = library()
+        B, A = mu.shape
+        args = [t.detach().contiguous().float() for t in (mu, std, value, actions, old_log_prob, old_mu, old_sigma,
+                                                           target_values, returns, advantages)]
+        scratch = torch.empty(lib.duck_ppo_loss_scratch(B, A), device=mu.device)
+        out = torch.empty(5, device=mu.device)
+        grad_mu, grad_std, grad_value = torch.empty_like(args[0]), torch.empty_like(args[1]), torch.empty_like(args[2])
+        P = lambda t: ctypes.c_void_p(t.data_ptr())
+        _raise(lib.duck_ppo_loss(B, A, *[P(t) for t in args], float(clip), float(value_coef), float(entropy_coef),
+                                 P(scratch), P(out), P(grad_mu), P(grad_std), P(grad_value), _stream(mu.device)))
+        ctx.grads = (grad_mu, grad_std, grad_value)
+        loss, stats = out[4], out[:4]
+        ctx.mark_non_differentiable(stats)
+        return loss, stats
+
+    @staticmethod
+    def backward(ctx, grad_loss, grad_stats):
+        gm, gs, gv = ctx.grads
+        return (gm * grad_loss, gs * grad_loss, gv * grad_loss) + (None,) * 10
+
+
 def ppo_loss(policy, obs, critic_obs, actions, old_log_prob, old_mu, old_sigma, target_values, returns, advantages,
              cfg: PPOConfig):
     """Clipped surrogate + clipped value loss - entropy bonus (rsl-rl
     PPO.update); also the mean KL of the new policy to the old one."""
+    if cfg.fused_loss and obs.is_cuda:
+        mu = policy.mean(obs)
+        value = policy.value(critic_obs)
+        loss, stats = FusedPPOLoss.apply(mu, policy.std, value, actions, old_log_prob, old_mu, old_sigma,
+                                         target_values, returns, advantages, cfg.clip, cfg.value_coef,
+                                         cfg.entropy_coef)
+        return loss, dict(surrogate=stats[0], value=stats[1], entropy=stats[2], kl=stats[3])
     dist_new = policy.distribution(obs)
     log_prob = dist_new.log_prob(actions).sum(-1)
     entropy = dist_new.entropy().sum(-1)

@@ -331,6 +331,23 @@ int duck_batch_set_parameters(duck_batch *batch, const void *mass, const void *i
  * since creation (for launch accounting in benchmarks). */
 int64_t duck_batch_launches(const duck_batch *batch);
 
+/* No reference counterpart in this repository: the loss of rsl-rl's PPO
+ * (third-party; the reference trains with it, scripts/train_bam_native.py:
+ * 14-140) for one minibatch, fused with its gradient.  Inputs are device
+ * float32 arrays: policy means mu [B,A], std [A], values [B], stored actions
+ * [B,A], old log-probabilities [B], old means and stds [B,A], rollout values,
+ * returns and normalised advantages [B].  Writes out[5] = (surrogate, value
+ * loss, entropy, kl, loss) and the loss gradient with respect to mu [B,A],
+ * std [A] and the values [B].  scratch holds duck_ppo_loss_scratch(B, A)
+ * floats.  Two kernel launches on `stream`, no allocation, no host sync: it
+ * can be captured in a CUDA graph.  A <= 32. */
+int duck_ppo_loss_scratch(int batch, int actions);
+int duck_ppo_loss(int batch, int actions, const float *mu, const float *std, const float *value, const float *act,
+                  const float *old_log_prob, const float *old_mu, const float *old_sigma, const float *target_value,
+                  const float *returns, const float *advantage, double clip, double value_coef,
+                  double entropy_coef, float *scratch, float *out, float *grad_mu, float *grad_std,
+                  float *grad_value, duck_stream stream);
+
 /* No reference counterpart.  FP32 fused-multiply-add throughput probe used
  * as the roofline denominator: runs `iterations` dependent FMA chains on
  * every SM and returns achieved TFLOP/s (2 flops per FMA) in *tflops. */

@@ -129,3 +129,67 @@ def test_gpu_update_matches_restatement(tmp_path):
     for k in agent.STATS:
         assert got[k] == pytest.approx(want[k], rel=2e-4, abs=2e-6), k
     assert agent.learning_rate == pytest.approx(kl_schedule_host(lr_before, got["kl"], cfg.desired_kl), rel=1e-12)
+
+
+def test_fused_loss_matches_torch_expression():
+    """duck_ppo_loss (fused CUDA loss and gradient) against the torch
+    expression of ppo_loss on the same minibatch: the loss and its statistics,
+    its gradient with respect to the policy means, std and values (all fp32),
+    and, through the bf16 MLPs, the gradient of every policy parameter."""
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+    from duck_gym_b200 import ppo
+
+    torch.manual_seed(5)
+    cfg = ppo.PPOConfig(actor_hidden=(64, 32), critic_hidden=(64, 32))
+    policy = ppo.ActorCritic(61, 76, 14, cfg).cuda()
+    B = 3000
+    g = torch.Generator(device="cuda").manual_seed(6)
+    r = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    obs, cobs = r(B, 61), r(B, 76)
+    with torch.no_grad():
+        old_mu = policy.mean(obs) + 0.05 * r(B, 14)
+    old_sigma = torch.full((B, 14), 0.15, device="cuda") * (1 + 0.1 * r(B, 14)).abs()
+    actions = old_mu + old_sigma * r(B, 14)
+    old_lp = torch.distributions.Normal(old_mu, old_sigma).log_prob(actions).sum(-1)
+    tv, ret, adv = r(B), r(B), r(B)
+    # The loss as a function of (mu, std, value): fused against torch.
+    with torch.no_grad():
+        mu0, v0 = policy.mean(obs), policy.value(cobs)
+    grads = []
+    for fused in (False, True):
+        mu = mu0.clone().requires_grad_(True)
+        std = policy.std.detach().clone().requires_grad_(True)
+        value = v0.clone().requires_grad_(True)
+        if fused:
+            loss, stats = ppo.FusedPPOLoss.apply(mu, std, value, actions, old_lp, old_mu, old_sigma, tv, ret, adv,
+                                                 cfg.clip, cfg.value_coef, cfg.entropy_coef)
+            stats = stats.tolist()
+        else:
+            d = torch.distributions.Normal(mu, std.expand(B, -1))
+            lp, ent = d.log_prob(actions).sum(-1), d.entropy().sum(-1)
+            ratio = torch.exp(lp - old_lp)
+            surr = torch.max(-adv * ratio, -adv * ratio.clamp(1 - cfg.clip, 1 + cfg.clip)).mean()
+            clipped = tv + (value - tv).clamp(-cfg.clip, cfg.clip)
+            vl = torch.max((value - ret).square(), (clipped - ret).square()).mean()
+            kl = (torch.log(std / old_sigma + 1e-5) + (old_sigma.square() + (old_mu - mu).square())
+                  / (2.0 * std.square()) - 0.5).sum(-1).mean()
+            loss = surr + cfg.value_coef * vl - cfg.entropy_coef * ent.mean()
+            stats = [float(surr), float(vl), float(ent.mean()), float(kl)]
+        loss.backward()
+        grads.append((float(loss.detach()), stats, mu.grad, std.grad, value.grad))
+    (l0, s0, *g0), (l1, s1, *g1) = grads
+    assert l1 == pytest.approx(l0, rel=1e-5, abs=1e-6)
+    assert s1 == pytest.approx(s0, rel=1e-5, abs=1e-6)
+    for a, b in zip(g0, g1):
+        torch.testing.assert_close(b, a, rtol=1e-4, atol=1e-9)
+    # Through the policy (bf16 MLPs): same parameter gradients up to bf16 rounding.
+    pg = []
+    for fused in (False, True):
+        cfg.fused_loss = fused
+        policy.zero_grad()
+        loss, _ = ppo.ppo_loss(policy, obs, cobs, actions, old_lp, old_mu, old_sigma, tv, ret, adv, cfg)
+        loss.backward()
+        pg.append([p.grad.detach().clone() for p in policy.parameters()])
+    for a, b in zip(*pg):
+        assert float((b - a).norm()) <= 1e-2 * float(a.norm()) + 1e-9
