@@ -159,10 +159,15 @@ template <class R, int T, bool P = true> struct Solver {
   Team<T> team;
   // This environment's randomised parameters (nullptr: the model's).
   const R *envMass = nullptr, *envInertia = nullptr, *envFriction = nullptr;
+  // 1 / dt and its square, divided once per launch (the compiler does not
+  // hoist the division out of the stamp loops on its own).
+  R ih, ih2;
 
   __device__ Solver(const DevModel<R> *model, const R *points, R *smemTeam, R *record, const Layout &layout)
       : m(model), pts(points), S{smemTeam}, rec(record), L(layout) {
     I = IntView<R, kTeams>{smemTeam + size_t(L.I) * kTeams};
+    ih = R(1) / m->dt;
+    ih2 = ih * ih;
   }
 
   // ------------------------------------------------------------ accessors
@@ -759,7 +764,6 @@ template <class R, int T, bool P = true> struct Solver {
   __device__ __forceinline__ void stampHinge(int bi, int j, const JointGeo &e, const Multipliers &mu, R *H, R *g, R kp,
                                              R limit) const {
     const R h = m->dt, alpha = m->alpha;
-    const R ih = R(1) / h, ih2 = ih * ih;
     const bool parent = e.a == bi;
     const R s = parent ? R(1) : R(-1);
     const R *lam = mu.lam, *pen = mu.pen;
@@ -870,7 +874,6 @@ template <class R, int T, bool P = true> struct Solver {
     const R h = m->dt;
     int item = 0;
     auto mine = [&]() { return kSplit == 1 || (item++ & 1) == part; };
-    const R ih = R(1) / h, ih2 = ih * ih;
     const R mass = massOf(bi);
 #pragma unroll
     for (int i = 0; i < 21; ++i) H[i] = R(0);
@@ -1242,8 +1245,8 @@ template <class R, int T, bool P = true> struct Solver {
         x0 = x0r[k];
         q0 = q0r[k];
       }
-      V3<R> v = (x - x0) * (R(1) / h);
-      V3<R> w = fqlog(qmul(quat(b), conj(q0))) * (R(1) / h);
+      V3<R> v = (x - x0) * ih;
+      V3<R> w = fqlog(qmul(quat(b), conj(q0))) * ih;
       SV vw = S + (L.XQP + 7 * b);
       vw[0] = v.x; vw[1] = v.y; vw[2] = v.z; vw[3] = w.x; vw[4] = w.y; vw[5] = w.z;
       if (!isfinite(dot(x, x) + dot(v, v) + dot(w, w))) bad = true;
