@@ -481,8 +481,8 @@ def run_extended(args, rank, world, local, device):
 
     if args.workload == "config4":
         return run_ppo(args, rank, world, local, device)
-    envs_total = args.envs if args.envs != ENVS else (16384 if args.workload == "config3" else 65536)
-    envs = weak_shard(envs_total * world, rank, world).count
+    per_gpu = args.envs if args.envs != ENVS else (16384 if args.workload == "config3" else 65536)
+    envs = weak_shard(per_gpu, rank, world).count   # weak scaling: envs per GPU fixed
     gen = torch.Generator(device=device).manual_seed(rank_seed(0, rank))
     stream = torch.cuda.current_stream(device)
     with tempfile.TemporaryDirectory() as d:
