@@ -679,30 +679,43 @@ def main():
         # End to end through the public API, every step: the step's targets
         # and forces copied in from pinned host memory, one step, the full
         # state() snapshot (bodies, joints, diagnostics) copied back to pinned
-        # host memory.
+        # host memory.  The copies run on two side streams (inputs, outputs)
+        # ordered by stream waits, so step k + 1 computes while step k's state
+        # goes back to the host (state() returns fresh tensors, which step
+        # k + 1 does not touch); the host buffers are double-buffered.
         host_in = torch.from_numpy(target_host).pin_memory()
         host_forces = torch.zeros(envs, 3).pin_memory()
         nb, nj = batch.num_bodies, batch.num_joints
-        host_bodies = torch.empty(envs, nb, 13).pin_memory()
-        host_joints = torch.empty(envs, nj, 2).pin_memory()
-        host_diag = torch.empty(envs, 6).pin_memory()
+        host_out = [(torch.empty(envs, nb, 13).pin_memory(), torch.empty(envs, nj, 2).pin_memory(),
+                     torch.empty(envs, 6).pin_memory()) for _ in range(2)]
+        inputs, outputs = torch.cuda.Stream(device), torch.cuda.Stream(device)
         e2e_steps = max(10, args.steps)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(e2e_steps):
-            tin = host_in.to(device, non_blocking=True)
-            fin = host_forces.to(device, non_blocking=True)
+        inputs.wait_stream(stream)
+        outputs.wait_stream(stream)
+        for k in range(e2e_steps):
+            with torch.cuda.stream(inputs):
+                tin = host_in.to(device, non_blocking=True)
+                fin = host_forces.to(device, non_blocking=True)
+            stream.wait_stream(inputs)
+            tin.record_stream(stream)
+            fin.record_stream(stream)
             batch.step(tin, fin, SUBSTEPS, kp, limit)
-            b, j, g = batch.state()
-            host_bodies.copy_(b, non_blocking=True)
-            host_joints.copy_(j, non_blocking=True)
-            host_diag.copy_(g, non_blocking=True)
+            state = batch.state()
+            outputs.wait_stream(stream)
+            with torch.cuda.stream(outputs):
+                for host, dev in zip(host_out[k % 2], state):
+                    host.copy_(dev, non_blocking=True)
+                    dev.record_stream(outputs)
+        stream.wait_stream(outputs)
         e1.record(stream)
         barrier()
         clocks.window = (t_start, time.monotonic())
         clocks.stop()
+        host_diag = host_out[(e2e_steps - 1) % 2][2]
         e2e_value = envs * SUBSTEPS * e2e_steps * world / max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
         failed_fraction = float((host_diag[:, 5] > 0).float().mean())
 
@@ -747,7 +760,7 @@ def main():
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": envs * (nj + 3) * 4,
                         "d2h_bytes_per_step": envs * (nb * 13 + nj * 2 + 6) * 4, "steps": e2e_steps,
                         "path": "CudaBatch.step + CudaBatch.state(): pinned host targets/forces in, bodies, joints "
-                                "and diag out, every step"},
+                                "and diag out, every step; copies on side streams overlap the next step"},
                 "gpu_launches": launches,
                 "clocks": clocks.summary((t_start, t_end)),
                 "clocks_all_regions": clocks.summary(),
