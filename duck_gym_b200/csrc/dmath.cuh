@@ -167,6 +167,32 @@ template <class M, class R> __device__ __forceinline__ V3<R> matVec(const M &m, 
   return {m[0] * v.x + m[1] * v.y + m[2] * v.z, m[3] * v.x + m[4] * v.y + m[5] * v.z,
           m[6] * v.x + m[7] * v.y + m[8] * v.z};
 }
+// atan2 for the solver's hinge angles and rotation logarithms, whose parity
+// bound is a tolerance: the ratio min(|x|, |y|) / max(|x|, |y|) in [0, 1], an
+// odd polynomial t P(t^2) for atan on [0, 1], then the octant and quadrant
+// restored.  P (degree 7 in t^2) was fitted for this file by iteratively
+// reweighted least squares on the relative error of atan(t) / t over
+// [0, 1]; evaluated in float its error is at most 1.6e-7 rad
+// (tests/test_fatan2.py checks it again over all four quadrants).
+__device__ __forceinline__ float fatan2(float y, float x) {
+  const float ax = fabsf(x), ay = fabsf(y);
+  const float mx = fmaxf(ax, ay), mn = fminf(ax, ay);
+  const float t = mx > 0.f ? mn * frcp(mx) : 0.f;
+  const float s = t * t;
+  float p = -0x1.33932ep-8f;
+  p = p * s + 0x1.8d589cp-6f;
+  p = p * s - 0x1.e74ea8p-5f;
+  p = p * s + 0x1.961640p-4f;
+  p = p * s - 0x1.1f1e4cp-3f;
+  p = p * s + 0x1.98fad4p-3f;
+  p = p * s - 0x1.5551d0p-2f;
+  p = p * s + 0x1.fffffcp-1f;
+  p *= t;
+  if (ay > ax) p = 1.57079632679489662f - p;
+  if (x < 0.f) p = 3.14159265358979324f - p;
+  return copysignf(p, y);
+}
+__device__ __forceinline__ double fatan2(double y, double x) { return atan2(y, x); }
 // Exponential map with fast normalisation (kernel.cuh:136-145).
 template <class R> __device__ __forceinline__ Q4<R> fqexp(V3<R> v) {
   R a2 = dot(v, v), a = fsqrt(a2), s, c;
@@ -180,6 +206,6 @@ template <class R> __device__ __forceinline__ V3<R> fqlog(Q4<R> q) {
   if (q.w < R(0)) q = {-q.w, -q.x, -q.y, -q.z};
   V3<R> v{q.x, q.y, q.z};
   R s = fnorm(v);
-  return v * (s < R(1e-10) ? R(2) : R(2) * atan2(s, q.w) * frcp(s));
+  return v * (s < R(1e-10) ? R(2) : R(2) * fatan2(s, q.w) * frcp(s));
 }
 }  // namespace duckb200

@@ -160,13 +160,21 @@ template <class R, int T, bool P = true> struct Solver {
   // This environment's randomised parameters (nullptr: the model's).
   const R *envMass = nullptr, *envInertia = nullptr, *envFriction = nullptr;
   // 1 / dt and its square, divided once per launch (the compiler does not
-  // hoist the division out of the stamp loops on its own).
+  // hoist the division out of the stamp loops on its own), and the model's
+  // solver constants, read once into registers instead of from the model in
+  // every stamp and dual update.
   R ih, ih2;
+  R sDt, sAlpha, sGamma, sBetaL, sBetaA;
 
   __device__ Solver(const DevModel<R> *model, const R *points, R *smemTeam, R *record, const Layout &layout)
       : m(model), pts(points), S{smemTeam}, rec(record), L(layout) {
     I = IntView<R, kTeams>{smemTeam + size_t(L.I) * kTeams};
     ih = R(1) / m->dt;
+    sDt = m->dt;
+    sAlpha = m->alpha;
+    sGamma = m->gamma;
+    sBetaL = m->betaLinear;
+    sBetaA = m->betaAngular;
     ih2 = ih * ih;
   }
 
@@ -595,7 +603,7 @@ template <class R, int T, bool P = true> struct Solver {
     e.C[3] = dot(e.t1, e.axisB);
     e.C[4] = dot(e.t2, e.axisB);
     V3<R> u = matVec(Rb, V3<R>{f[15], f[16], f[17]});
-    e.angle = atan2(dot(e.axis, cross(e.t1, u)), dot(e.t1, u));
+    e.angle = fatan2(dot(e.axis, cross(e.t1, u)), dot(e.t1, u));
     e.C[5] = e.angle - f[18];
     e.C[6] = f[19] - e.angle;
   }
@@ -763,7 +771,7 @@ template <class R, int T, bool P = true> struct Solver {
   // damping/armature and dry friction summed along the hinge axis.
   __device__ __forceinline__ void stampHinge(int bi, int j, const JointGeo &e, const Multipliers &mu, R *H, R *g, R kp,
                                              R limit) const {
-    const R h = m->dt, alpha = m->alpha;
+    const R h = sDt, alpha = sAlpha;
     const bool parent = e.a == bi;
     const R s = parent ? R(1) : R(-1);
     const R *lam = mu.lam, *pen = mu.pen;
@@ -826,7 +834,7 @@ template <class R, int T, bool P = true> struct Solver {
   // in the contact basis.  A member function (not a lambda) so that H and g
   // stay in registers.
   __device__ __forceinline__ void stampContact(int bi, int ci, V3<R> x, SV Rb, int nGround, R *H, R *g) const {
-    const R alpha = m->alpha;
+    const R alpha = sAlpha;
     const int meta = cmeta(ci);
     const int body = metaBody(meta), other = metaOther(meta);
     const SV c = contact(ci);
@@ -989,7 +997,7 @@ template <class R, int T, bool P = true> struct Solver {
   // Dual update of hinge j (kernel.cuh:991-1028): multipliers, penalty ramps,
   // dry friction; folds the constraint error into *error.
   __device__ __forceinline__ void dualHinge(int j, const JointGeo &e, R &error, Multipliers &mu) const {
-    const R alpha = m->alpha;
+    const R alpha = sAlpha;
     const SV lam = S + (L.JL + 7 * j), pen = S + (L.JP + 7 * j), c0 = S + (L.JC0 + 7 * j);
     const int rows = e.limited ? 7 : 5;
 #pragma unroll
@@ -1000,7 +1008,7 @@ template <class R, int T, bool P = true> struct Solver {
       mu.lam[k] = k >= 5 ? rmin(f, R(0)) : f;
       lam[k] = mu.lam[k];
       if (k < 5 || f < R(0)) {
-        mu.pen[k] = rmin(mu.pen[k] + (k < 3 ? m->betaLinear : m->betaAngular) * fabs(c), k < 3 ? R(1e9) : R(1e7));
+        mu.pen[k] = rmin(mu.pen[k] + (k < 3 ? sBetaL : sBetaA) * fabs(c), k < 3 ? R(1e9) : R(1e7));
         pen[k] = mu.pen[k];
       }
       error = rmax(error, k < 5 ? R(fabs(c)) : rmax(R(0), -c));
@@ -1011,7 +1019,7 @@ template <class R, int T, bool P = true> struct Solver {
       R trial = mu.lf + mu.pf * delta;
       R lf = rclamp(trial, -fl, fl);
       R pf = mu.pf;
-      if (fabs(trial) < fl) pf = rmin(pf + m->betaAngular * R(fabs(delta)), R(1e7));
+      if (fabs(trial) < fl) pf = rmin(pf + sBetaA * R(fabs(delta)), R(1e7));
       mu.lf = lf;
       mu.pf = pf;
       S[L.JLF + j] = lf;
@@ -1038,7 +1046,7 @@ template <class R, int T, bool P = true> struct Solver {
       C = {dot(delta, V3<R>{bs[0], bs[1], bs[2]}), dot(delta, V3<R>{bs[3], bs[4], bs[5]}),
            dot(delta, V3<R>{bs[6], bs[7], bs[8]})};
     }
-    C.z -= m->alpha * c[cC0];
+    C.z -= sAlpha * c[cC0];
     return C;
   }
 
@@ -1217,7 +1225,7 @@ template <class R, int T, bool P = true> struct Solver {
         for (int k = 0; k < 3; ++k) {
           c[cLambda + k] = fk[k];
           if (f.z < R(0) && (k == 2 || cone))
-            c[cPenalty + k] = rmin(c[cPenalty + k] + m->betaLinear * R(fabs(Ck[k])), R(1e9));
+            c[cPenalty + k] = rmin(c[cPenalty + k] + sBetaL * R(fabs(Ck[k])), R(1e9));
         }
         error = rmax(error, rmax(R(0), -C.z));
       }

@@ -7,6 +7,9 @@ times.
   call.
 * The self-contact workload: 16384 envs of the 91-pair biped, a few
   substeps teacher-forced against the raised-limit oracle.
+* The domain-randomised workload: 65536 envs at 20 iterations with per-env
+  parameters, one substep of the whole batch, checked on 32 envs spread over
+  it against one-env oracle batches carrying each env's values.
 * The CPU-runnable workload as written: 16 envs, 1000 control steps of HOME +
   N(0, 0.1 rad) targets drawn per joint per step, ensemble statistics (mean
   base height, joint RMS, contact count) within 1 % of the oracle's.
@@ -33,10 +36,10 @@ THREADS = min(64, os.cpu_count() or 1)
 POSE_TOL = 1e-4
 
 
-def oracle(model, n, **kw):
+def oracle(model, n, iterations=10, **kw):
     from oracle.oracle import OracleBatch
 
-    return OracleBatch(model, n, 0.005, 10, threads=THREADS, **kw)
+    return OracleBatch(model, n, 0.005, iterations, threads=THREADS, **kw)
 
 
 def bench_targets(meta, envs):
@@ -177,3 +180,58 @@ def test_cpu_runnable_workload_1000_steps(biped_model, biped_meta):
     g = np.mean(stats["gpu"], axis=0)
     print(f"oracle (height, joint RMS, contacts) {o}, GPU {g}")
     np.testing.assert_allclose(g, o, rtol=0.01)
+
+
+def test_domain_randomized_65536_envs_sample(tmp_path, biped_model, biped_meta):
+    """The domain-randomised launch shape: 65536 envs at 20 iterations with
+    per-env masses, inertias and ground frictions, joint-offset resets and
+    base pushes for 20 control steps; then one substep of the whole batch
+    from its own state, checked on 32 envs spread over the batch against
+    one-env oracle batches built from model files carrying each env's values."""
+    from duck_gym_b200 import CudaBatch, biped
+    from test_gpu_extensions import randomized
+
+    envs, sample = 65536, np.linspace(0, 65535, 32).astype(int)
+    kp, limit = biped_meta["kp"], biped_meta["torque_limit"]
+    text, mass, inertia, friction = randomized(biped_model, envs, seed=21)
+    gpu = CudaBatch(str(biped_model), envs, 0.005, 20)
+    gpu.set_parameters(dev(mass), dev(inertia), dev(friction))
+    q = helpers.home_q(biped_meta, envs, noise=0.02, seed=22)
+    gpu.reset(torch.ones(envs, dtype=torch.bool, device="cuda"), dev(q), torch.zeros(envs, 6, device="cuda"))
+    target = dev(helpers.targets(biped_meta, 1, envs, 0.05, seed=23)[0])
+    rng = np.random.default_rng(24)
+    for _ in range(20):
+        push = (rng.random((envs, 1)) < 0.02) * rng.normal(0, 0.5, (envs, 3)) * mass[:, 1:2] / (4 * 0.005)
+        gpu.step(target, dev(push.astype(np.float32)), 4, kp, limit)
+    start = gpu.export_records().cpu().numpy()
+    t = target.cpu().numpy()
+    zero = torch.zeros(envs, 3, device="cuda")
+    gpu.step(target, zero, 1, kp, limit)
+    grec = gpu.export_records().cpu().numpy()
+    gb, gj, gd = [x.cpu().numpy() for x in gpu.state()]
+    stats, poses = VelocityStats(), helpers.VelocityStats(POSE_TOL, floor=0.0)
+    nb, nj = gpu.num_bodies, gpu.num_joints
+    for e in sample:
+        path = tmp_path / f"env{e}.duck"
+        path.write_text(biped.with_parameters(text, mass[e], inertia[e], friction[e]))
+        make = lambda: oracle(path, 1, iterations=20)
+        ora = make()
+        ora.import_env(0, start[e])
+        twins = helpers.UlpTwins(make)
+        step = lambda b: b.step(t[e:e + 1], np.zeros((1, 3), np.float32), 1, kp, limit)
+        tw = twins.advance(start[e:e + 1], step)
+        step(ora)
+        ob, oj, od = ora.state()
+        np.testing.assert_array_equal(helpers.contact_keys_from_records(grec[e:e + 1], nb, nj)[0],
+                                      helpers.contact_keys_from_records(ora.export_env(0)[None], nb, nj)[0],
+                                      err_msg=f"contact set of env {e}")
+        assert gd[e, 5] == od[0, 5] and gd[e, 2] == od[0, 2]
+        if od[0, 5]:
+            continue
+        poses.add("body pose", gb[e, :, :7], ob[0, :, :7], [x[0][0, :, :7] for x in tw])
+        poses.add("joint angle", gj[e, :, 0], oj[0, :, 0], [x[1][0, :, 0] for x in tw])
+        stats.add("body velocity", gb[e, :, 7:], ob[0, :, 7:], [x[0][0, :, 7:] for x in tw])
+        stats.add("joint rate", gj[e, :, 1], oj[0, :, 1], [x[1][0, :, 1] for x in tw])
+    stats.check()
+    poses.check()
+    assert np.abs(gb[sample[0], 1, :3] - gb[sample[1], 1, :3]).max() > 1e-6
