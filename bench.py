@@ -690,33 +690,43 @@ def main():
                      torch.empty(envs, 6).pin_memory()) for _ in range(2)]
         inputs, outputs = torch.cuda.Stream(device), torch.cuda.Stream(device)
         e2e_steps = max(10, args.steps)
-        barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        inputs.wait_stream(stream)
-        outputs.wait_stream(stream)
-        for k in range(e2e_steps):
-            with torch.cuda.stream(inputs):
-                tin = host_in.to(device, non_blocking=True)
-                fin = host_forces.to(device, non_blocking=True)
-            stream.wait_stream(inputs)
-            tin.record_stream(stream)
-            fin.record_stream(stream)
-            batch.step(tin, fin, SUBSTEPS, kp, limit)
-            state = batch.state()
-            outputs.wait_stream(stream)
-            with torch.cuda.stream(outputs):
-                for host, dev in zip(host_out[k % 2], state):
-                    host.copy_(dev, non_blocking=True)
-                    dev.record_stream(outputs)
-        stream.wait_stream(outputs)
-        e1.record(stream)
-        barrier()
+        # The clock record covers the timed steps and the trials; the sampler
+        # stops before the end-to-end pass, whose host thread issues every
+        # copy and launch itself.
         clocks.window = (t_start, time.monotonic())
         clocks.stop()
+
+        def e2e_window():
+            barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            inputs.wait_stream(stream)
+            outputs.wait_stream(stream)
+            for k in range(e2e_steps):
+                with torch.cuda.stream(inputs):
+                    tin = host_in.to(device, non_blocking=True)
+                    fin = host_forces.to(device, non_blocking=True)
+                stream.wait_stream(inputs)
+                tin.record_stream(stream)
+                fin.record_stream(stream)
+                batch.step(tin, fin, SUBSTEPS, kp, limit)
+                state = batch.state()
+                outputs.wait_stream(stream)
+                with torch.cuda.stream(outputs):
+                    for host, dev in zip(host_out[k % 2], state):
+                        host.copy_(dev, non_blocking=True)
+                        dev.record_stream(outputs)
+            stream.wait_stream(outputs)
+            e1.record(stream)
+            barrier()
+            return envs * SUBSTEPS * e2e_steps * world / max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
+
+        # Three windows, median: one window is short enough for a stall of
+        # the shared host to dominate it.
+        e2e_values = [e2e_window() for _ in range(3)]
         host_diag = host_out[(e2e_steps - 1) % 2][2]
-        e2e_value = envs * SUBSTEPS * e2e_steps * world / max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
+        e2e_value = statistics.median(e2e_values)
         failed_fraction = float((host_diag[:, 5] > 0).float().mean())
 
         line = None
@@ -759,6 +769,7 @@ def main():
                                                              "between steps, max over ranks"},
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": envs * (nj + 3) * 4,
                         "d2h_bytes_per_step": envs * (nb * 13 + nj * 2 + 6) * 4, "steps": e2e_steps,
+                        "windows": e2e_values, "statistic": "median of 3 windows",
                         "path": "CudaBatch.step + CudaBatch.state(): pinned host targets/forces in, bodies, joints "
                                 "and diag out, every step; copies on side streams overlap the next step"},
                 "gpu_launches": launches,
