@@ -48,10 +48,19 @@ def load_oracle_state(gpu, ora):
     gpu.import_records(dev(rec))
 
 
-def VelocityStats(tol=VEL_TOL):
+class VelocityStats(helpers.VelocityStats):
     """Velocity differences pooled per test and held to the one-ulp envelope
-    of the reference algorithm measured on the same checks (helpers.py)."""
-    return helpers.VelocityStats(tol)
+    of the reference algorithm measured on the same checks (helpers.py); the
+    poses likewise, with `pose_tol` and no floor, so with twins that stay
+    within it the plain pose bound applies (up to three components)."""
+
+    def __init__(self, tol=VEL_TOL, pose_tol=POSE_TOL):
+        super().__init__(tol)
+        self.poses = helpers.VelocityStats(pose_tol, floor=0.0)
+
+    def check(self):
+        super().check()
+        self.poses.check()
 
 
 def twins_for(model, n, dt, iterations, **kw):
@@ -59,7 +68,7 @@ def twins_for(model, n, dt, iterations, **kw):
     return helpers.UlpTwins(lambda: oracle(model, n, dt, iterations, **kw))
 
 
-def compare_substep(gpu, ora, stats, twin_states=(), pose_tol=POSE_TOL, diag_tol=1e-4):
+def compare_substep(gpu, ora, stats, twin_states=(), diag_tol=1e-4):
     gb, gj, gd = host_state(gpu)
     ob, oj, od = ora.state()
     np.testing.assert_array_equal(gd[:, 5], od[:, 5], err_msg="failure flags differ")
@@ -67,8 +76,8 @@ def compare_substep(gpu, ora, stats, twin_states=(), pose_tol=POSE_TOL, diag_tol
     for e in range(ora.num_envs):
         np.testing.assert_array_equal(gpu.contact_keys(e), ora.contact_keys(e),
                                       err_msg=f"contact set of env {e} differs")
-    np.testing.assert_allclose(gb[live][..., :7], ob[live][..., :7], rtol=0, atol=pose_tol)
-    np.testing.assert_allclose(gj[live][..., 0], oj[live][..., 0], rtol=0, atol=pose_tol)
+    stats.poses.add("body pose", gb[live][..., :7], ob[live][..., :7], [t[0][live][..., :7] for t in twin_states])
+    stats.poses.add("joint angle", gj[live][..., 0], oj[live][..., 0], [t[1][live][..., 0] for t in twin_states])
     stats.add("body velocity", gb[live][..., 7:], ob[live][..., 7:], [t[0][live][..., 7:] for t in twin_states])
     stats.add("joint rate", gj[live][..., 1], oj[live][..., 1], [t[1][live][..., 1] for t in twin_states])
     np.testing.assert_array_equal(gd[live][:, 2], od[live][:, 2])
@@ -287,12 +296,12 @@ def test_fp64_single_substep(cuda, biped_model, biped_meta):
     ora = oracle(biped_model, n, 0.005, 10, fp64=True)
     t = helpers.targets(biped_meta, steps, n, 0.1, seed=9).astype(np.float64)
     f = np.zeros((n, 3))
-    stats = VelocityStats(tol=1e-6)
+    stats = VelocityStats(tol=1e-6, pose_tol=1e-8)
     twins = twins_for(biped_model, n, 0.005, 10, fp64=True)
     for s in range(steps):
         if s % 6 == 5:
             teacher_check(gpu, ora, twins, lambda: gpu.step(dev(t[s]), dev(f), 1, kp, limit),
-                          lambda b: b.step(t[s], f, 1, kp, limit), stats, pose_tol=1e-8, diag_tol=1e-8)
+                          lambda b: b.step(t[s], f, 1, kp, limit), stats, diag_tol=1e-8)
         ora.step(t[s], f, 4, kp, limit)
     stats.check()
 
