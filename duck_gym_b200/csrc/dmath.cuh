@@ -194,23 +194,23 @@ __device__ __forceinline__ float fatan2(float y, float x) {
 }
 __device__ __forceinline__ double fatan2(double y, double x) { return atan2(y, x); }
 // Exponential map with fast normalisation (kernel.cuh:136-145).
-// sin and cos of a half rotation angle: below 0.125 rad (every clamped
-// Gauss-Seidel step, whose rotation is at most 0.25 rad, and the predictor
-// at ordinary spin rates) the Taylor series to h^7 / h^6 in float, whose
-// truncation error (h^9 / 9!, h^8 / 8!) is below 1e-11; above, sincos.
-template <class R> __device__ __forceinline__ void sincosHalf(R h, R *s, R *c) {
-  if (sizeof(R) == 4 && fabs(h) <= R(0.125)) {
-    const R h2 = h * h;
-    *s = h * (R(1) + h2 * (R(-1.0 / 6) + h2 * (R(1.0 / 120) - h2 * R(1.0 / 5040))));
-    *c = R(1) + h2 * (R(-0.5) + h2 * (R(1.0 / 24) - h2 * R(1.0 / 720)));
-  } else {
-    sincosT(h, s, c);
-  }
-}
+// Below 0.25 rad (every clamped Gauss-Seidel step, whose rotation is at most
+// 0.25 rad, and the predictor at ordinary spin rates) cos(a/2) and
+// sin(a/2)/a come from their Taylor series in a^2 to the a^6 terms, in float,
+// with no square root (truncation error below 1e-11); above, sincos.
 template <class R> __device__ __forceinline__ Q4<R> fqexp(V3<R> v) {
-  R a2 = dot(v, v), a = fsqrt(a2), s, c;
-  sincosHalf(a * R(0.5), &s, &c);
-  R k = a < R(1e-8) ? R(0.5) - a2 / R(48) : s * frcp(a);
+  const R a2 = dot(v, v);
+  R c, k;
+  if (sizeof(R) == 4 && a2 <= R(0.0625)) {
+    const R h2 = R(0.25) * a2;
+    k = R(0.5) * (R(1) + h2 * (R(-1.0 / 6) + h2 * (R(1.0 / 120) - h2 * R(1.0 / 5040))));
+    c = R(1) + h2 * (R(-0.5) + h2 * (R(1.0 / 24) - h2 * R(1.0 / 720)));
+  } else {
+    const R a = fsqrt(a2);
+    R s;
+    sincosT(a * R(0.5), &s, &c);
+    k = a < R(1e-8) ? R(0.5) - a2 / R(48) : s * frcp(a);
+  }
   return fnormalized(Q4<R>{c, k * v.x, k * v.y, k * v.z});
 }
 // Logarithm of a (near) unit quaternion (kernel.cuh:146-153).

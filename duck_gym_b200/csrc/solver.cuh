@@ -603,7 +603,7 @@ template <class R, int T, bool P = true> struct Solver {
     e.C[3] = dot(e.t1, e.axisB);
     e.C[4] = dot(e.t2, e.axisB);
     V3<R> u = matVec(Rb, V3<R>{f[15], f[16], f[17]});
-    e.angle = fatan2(dot(e.axis, cross(e.t1, u)), dot(e.t1, u));
+    e.angle = fatan2(dot(e.t2, u), dot(e.t1, u));
     e.C[5] = e.angle - f[18];
     e.C[6] = f[19] - e.angle;
   }
@@ -699,19 +699,18 @@ template <class R, int T, bool P = true> struct Solver {
     }
     return f;
   }
-  // SO(3) log-Jacobian coefficient (1 - (a/2) cot(a/2)) / a^2, from its
-  // Bernoulli series below 0.5 rad (relative error < 1e-12 there) and from the
-  // closed form above, where it has no cancellation.
-  static __device__ __forceinline__ R logJacobianCoef(R a) {
-    if (a < R(0.5)) {
-      R a2 = a * a;
+  // SO(3) log-Jacobian coefficient (1 - (a/2) cot(a/2)) / a^2 as a function
+  // of a^2: its Bernoulli series below 0.5 rad (relative error < 1e-12 there,
+  // no square root) and the closed form above, where it has no cancellation.
+  static __device__ __forceinline__ R logJacobianCoef(R a2) {
+    if (a2 < R(0.25)) {
       return R(1.0 / 12) + a2 * (R(1.0 / 720) + a2 * (R(1.0 / 30240) + a2 * (R(1.0 / 1209600) +
                                                                                a2 * R(1.0 / 47900160))));
     }
-    R h = R(0.5) * a;
+    const R a = fsqrt(a2), h = R(0.5) * a;
     R s, c;
     sincosT(h, &s, &c);
-    return (R(1) - h * c / s) / (a * a);
+    return (R(1) - h * c / s) / a2;
   }
   // Solve H x = -g with a packed Cholesky factorisation (kernel.cuh:177-228);
   // false on a non-positive pivot.
@@ -895,8 +894,8 @@ template <class R, int T, bool P = true> struct Solver {
       R ml = mass * ih2;
       H[tri(0, 0)] = ml; H[tri(1, 1)] = ml; H[tri(2, 2)] = ml;
       g[0] = ml * dx.x; g[1] = ml * dx.y; g[2] = ml * dx.z;
-      R a2 = dot(th, th), a = fsqrt(a2);
-      R coef = logJacobianCoef(a);
+      R a2 = dot(th, th);
+      R coef = logJacobianCoef(a2);
       // rotJ[k] = e_k - theta x e_k / 2 + coef theta x (theta x e_k), as columns.
       R J[3][3];
       R d = R(1) - coef * a2;
@@ -978,7 +977,8 @@ template <class R, int T, bool P = true> struct Solver {
   }
 
   // Solve H st = -g, clamp the step (0.1 m, 0.25 rad) and move body bi;
-  // returns the applied step length (kernel.cuh:928-936).
+  // returns the square of the applied step length (kernel.cuh:928-936).  An
+  // unclamped step (the usual case) needs no square root or reciprocal.
   __device__ __forceinline__ R applyBody(int bi, const R (&H)[21], const R (&g)[6], int part) {
     const V3<R> x = ld3(L.X + 3 * bi);
     const Q4<R> q = quat(bi);
@@ -988,10 +988,14 @@ template <class R, int T, bool P = true> struct Solver {
       for (int i = 0; i < 6; ++i) st[i] = R(NAN);
     }
     V3<R> tx{st[0], st[1], st[2]}, rx{st[3], st[4], st[5]};
-    R nt = fnorm(tx), nr = fnorm(rx);
-    R scale = rmin(R(1), rmin(R(.1) * frcp(rmax(nt, R(1e-30))), R(.25) * frcp(rmax(nr, R(1e-30)))));
+    const R nt2 = dot(tx, tx), nr2 = dot(rx, rx);
+    R scale = R(1);
+    if (nt2 > R(0.01) || nr2 > R(0.0625)) {
+      const R nt = fsqrt(nt2), nr = fsqrt(nr2);
+      scale = rmin(R(1), rmin(R(.1) * frcp(rmax(nt, R(1e-30))), R(.25) * frcp(rmax(nr, R(1e-30)))));
+    }
     if (part == 0) setPose(bi, x + tx * scale, fnormalized(qmul(fqexp(rx * scale), q)));
-    return rmax(nt, nr) * scale;
+    return rmax(nt2, nr2) * scale * scale;
   }
 
   // Dual update of hinge j (kernel.cuh:991-1028): multipliers, penalty ramps,
@@ -1232,7 +1236,8 @@ template <class R, int T, bool P = true> struct Solver {
       error = team.max(error);
       team.sync();
       diag.iterations = it + 1;
-      diag.converged = maxUpdate < tol && error < tol;
+      // maxUpdate holds squared step lengths.
+      diag.converged = maxUpdate < tol * tol && error < tol;
       if (diag.converged) break;
     }
     // Velocity recovery (kernel.cuh:1064-1073); the velocities return to the
