@@ -445,8 +445,102 @@ template <class R, int T, bool P = true> struct Solver {
     }
     return n;
   }
-  // Ground contact with warm start from the record (kernel.cuh:618-650).
-  __device__ void buildGround(int slot, int s, int best, V3<R> bestWorld, int prevCount) {
+  // Warm-start data of a previous ground contact, read from the record.
+  struct WarmStart {
+    R lambda[3], penalty[3];
+    V3<R> local, anchor;
+    bool found, stick;
+  };
+  // Ground contact with warm start (kernel.cuh:618-650).
+  __device__ __forceinline__ void buildGround(int slot, int s, int best, V3<R> bestWorld, const WarmStart &w) {
+    const int b = ldg(m->sBody[s]);
+    V3<R> x = ld3(L.X + 3 * b);
+    Q4<R> q = quat(b);
+    V3<R> local = xpoint(s, q, best);
+    V3<R> anchor{bestWorld.x, bestWorld.y, R(0)};
+    R lambda[3] = {R(0), R(0), R(0)}, penalty[3] = {R(1000), R(1000), R(1000)};
+    if (w.found) {
+#pragma unroll
+      for (int d = 0; d < 3; ++d) { lambda[d] = w.lambda[d]; penalty[d] = w.penalty[d]; }
+      if (w.stick) {
+        local = w.local;
+        anchor = w.anchor;
+      }
+    }
+    const R c0 = rmin(xadd(x, xrotate(q, local)).z, R(0));
+    const R ag = xmul(m->alpha, m->gamma);
+    SV c = contact(slot);
+    cmeta(slot) = packMeta(b, -1, s, -1);
+    cfeat(slot) = best;
+    c[cLocal] = local.x; c[cLocal + 1] = local.y; c[cLocal + 2] = local.z;
+    c[cAnchor] = anchor.x; c[cAnchor + 1] = anchor.y; c[cAnchor + 2] = anchor.z;
+    c[cFriction] = frictionOf(s);
+    c[cC0] = c0;
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      c[cLambda + d] = xmul(lambda[d], ag);
+      c[cPenalty + d] = rclamp(xmul(penalty[d], m->gamma), R(1000), R(1e9));
+    }
+  }
+  // Warm-start entry of a pick: the first previous contact with the same
+  // shape and feature, read from the record.
+  __device__ __forceinline__ WarmStart warmStart(int match) const {
+    WarmStart w;
+    w.found = match >= 0;
+    if (w.found) {
+      const R *p = rec + kRecHeader + kRecBody * m->nb + kRecJoint * m->nj + kRecContact * match;
+#pragma unroll
+      for (int d = 0; d < 3; ++d) { w.lambda[d] = p[26 + d]; w.penalty[d] = p[29 + d]; }
+      w.stick = p[5] != R(0);
+      w.local = {p[6], p[7], p[8]};
+      w.anchor = {p[9], p[10], p[11]};
+    }
+    return w;
+  }
+  // The ground contacts of one shape's n picks.  Without body pairs the
+  // warm-start entries of all picks are looked up first and their record
+  // reads issued together, so the picks wait for one round trip to the
+  // record instead of one each; the pair instantiation, short of registers,
+  // keeps one pick at a time.
+  __device__ __forceinline__ void buildGroundPicks(int s, int n, const int (&feature)[4], const V3<R> (&world)[4],
+                                                   int first, int prevCount) {
+    if constexpr (!P) {
+      int key[4], match[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        key[k] = k < n ? groundKey(s, feature[k]) : -2;
+        match[k] = -1;
+      }
+      for (int i = 0; i < prevCount; ++i) {
+        const int have = I[L.prevKeys + i];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (match[k] < 0 && have == key[k]) match[k] = i;
+      }
+      WarmStart w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) w[k] = warmStart(match[k]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (k >= n) break;
+        const int slot = first + k;
+        if (slot < L.cap) buildGround(slot, s, feature[k], world[k], w[k]);
+        else I[iFailed] = 1;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (k >= n) break;
+        const int slot = first + k;
+        if (slot < L.cap) buildGroundSearch(slot, s, feature[k], world[k], prevCount);
+        else I[iFailed] = 1;
+      }
+    }
+  }
+
+  // Ground contact with warm start from the record, searched and read for
+  // one pick at a time (kernel.cuh:618-650): the pair instantiation.
+  __device__ void buildGroundSearch(int slot, int s, int best, V3<R> bestWorld, int prevCount) {
     const int b = ldg(m->sBody[s]);
     V3<R> x = ld3(L.X + 3 * b);
     Q4<R> q = quat(b);
@@ -511,13 +605,7 @@ template <class R, int T, bool P = true> struct Solver {
       int n = s < m->ns ? groundPicks(s, feature, world) : 0;
       int total;
       int offset = team.scan(n, &total);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (k >= n) break;
-        int slot = base + offset + k;
-        if (slot < L.cap) buildGround(slot, s, feature[k], world[k], prevCount);
-        else I[iFailed] = 1;
-      }
+      if (n > 0) buildGroundPicks(s, n, feature, world, base + offset, prevCount);
       base += total;
     }
     base = base < L.cap ? base : L.cap;
