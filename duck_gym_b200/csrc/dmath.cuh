@@ -198,7 +198,11 @@ __device__ __forceinline__ double fatan2(double y, double x) { return atan2(y, x
 // 0.25 rad, and the predictor at ordinary spin rates) cos(a/2) and
 // sin(a/2)/a come from their Taylor series in a^2 to the a^6 terms, in float,
 // with no square root (truncation error below 1e-11); above, sincos.
-template <class R> __device__ __forceinline__ Q4<R> fqexp(V3<R> v) {
+// fqexpRaw leaves the result unnormalised, for callers that normalise the
+// product they form with it; fqexp normalises.
+template <class R> __device__ __forceinline__ Q4<R> fqexpRaw(V3<R> v);
+template <class R> __device__ __forceinline__ Q4<R> fqexp(V3<R> v) { return fnormalized(fqexpRaw(v)); }
+template <class R> __device__ __forceinline__ Q4<R> fqexpRaw(V3<R> v) {
   const R a2 = dot(v, v);
   R c, k;
   if (sizeof(R) == 4 && a2 <= R(0.0625)) {
@@ -211,11 +215,13 @@ template <class R> __device__ __forceinline__ Q4<R> fqexp(V3<R> v) {
     sincosT(a * R(0.5), &s, &c);
     k = a < R(1e-8) ? R(0.5) - a2 / R(48) : s * frcp(a);
   }
-  return fnormalized(Q4<R>{c, k * v.x, k * v.y, k * v.z});
+  return Q4<R>{c, k * v.x, k * v.y, k * v.z};
 }
-// Logarithm of a (near) unit quaternion (kernel.cuh:146-153).
+// Logarithm of a (near) unit quaternion (kernel.cuh:146-153).  The result
+// depends on q only through the direction of its vector part and the angle
+// atan2(|v|, w), both unchanged by a positive scale, so q is not normalised
+// first.
 template <class R> __device__ __forceinline__ V3<R> fqlog(Q4<R> q) {
-  q = fnormalized(q);
   if (q.w < R(0)) q = {-q.w, -q.x, -q.y, -q.z};
   V3<R> v{q.x, q.y, q.z};
   R s = fnorm(v);

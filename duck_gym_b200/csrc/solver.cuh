@@ -1082,7 +1082,7 @@ template <class R, int T, bool P = true> struct Solver {
       const R nt = fsqrt(nt2), nr = fsqrt(nr2);
       scale = rmin(R(1), rmin(R(.1) * frcp(rmax(nt, R(1e-30))), R(.25) * frcp(rmax(nr, R(1e-30)))));
     }
-    if (part == 0) setPose(bi, x + tx * scale, fnormalized(qmul(fqexp(rx * scale), q)));
+    if (part == 0) setPose(bi, x + tx * scale, fnormalized(qmul(fqexpRaw(rx * scale), q)));
     return rmax(nt2, nr2) * scale * scale;
   }
 
