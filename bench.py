@@ -264,6 +264,53 @@ def cpu_baseline(model, meta, seconds=12.0, envs=1024):
                       f"({SUBSTEPS} substeps), wall clock"}
 
 
+def small_batch(model, meta, device, envs=16, steps=1000):
+    """The CPU-runnable workload as written: 16 envs from HOME, HOME + N(0,
+    0.1 rad) targets drawn per joint per control step, 1000 control steps of
+    4 substeps.  Timed on the reference's CPU solver (one thread per env, as
+    many as the host has, wall clock) and on this library (the targets
+    already on the device, CUDA events around the 1000 launches): a batch
+    this small leaves the GPU launch-bound, which is what the number shows."""
+    import torch
+
+    from duck_gym_b200 import CudaBatch
+
+    rng = np.random.default_rng(0)
+    home = np.asarray(meta["home"], np.float32)
+    targets = (home + rng.normal(0, 0.1, (steps, envs, home.size))).astype(np.float32)
+    forces = np.zeros((envs, 3), np.float32)
+    q = np.tile(home, (envs, 1))
+    cores = min(envs, os.cpu_count() or 1)
+    cpu, kind = reference_batch(model, envs, cores)
+    cpu.reset(np.ones(envs, bool), q, np.zeros((envs, 6), np.float32))
+    t0 = time.perf_counter()
+    for k in range(steps):
+        cpu.step(targets[k], forces, SUBSTEPS, meta["kp"], meta["torque_limit"])
+    cpu_value = envs * SUBSTEPS * steps / (time.perf_counter() - t0)
+    gpu = CudaBatch(model, envs, DT, ITERATIONS, device.index)
+    gpu.reset(torch.ones(envs, dtype=torch.bool, device=device), torch.from_numpy(q).to(device),
+              torch.zeros(envs, 6, device=device))
+    dt_targets = torch.from_numpy(targets).to(device)
+    df = torch.zeros(envs, 3, device=device)
+    for k in range(5):
+        gpu.step(dt_targets[k], df, SUBSTEPS, meta["kp"], meta["torque_limit"])
+    gpu.reset(torch.ones(envs, dtype=torch.bool, device=device), torch.from_numpy(q).to(device),
+              torch.zeros(envs, 6, device=device))
+    stream = torch.cuda.current_stream(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    a.record(stream)
+    for k in range(steps):
+        gpu.step(dt_targets[k], df, SUBSTEPS, meta["kp"], meta["torque_limit"])
+    b.record(stream)
+    b.synchronize()
+    gpu_value = envs * SUBSTEPS * steps / (a.elapsed_time(b) / 1e3)
+    return {"workload": f"{envs} envs from HOME, HOME + N(0,0.1 rad) targets per joint per control step, "
+                        f"{steps} control steps", "unit": UNIT,
+            "cpu": {"value": cpu_value, "cores": cores, "kind": kind, "timing": "wall clock"},
+            "gpu": {"value": gpu_value, "timing": "CUDA events, targets resident on the device"}}
+
+
 def reference_cuda_module():
     """The reference's own CUDA extension rebuilt for sm_100a by
     oracle/build_ref_cuda.py, or None."""
@@ -783,6 +830,7 @@ def main():
             }
             if not args.no_cpu_baseline and world == 1:
                 line["cpu_baseline"] = cpu_baseline(model, meta)
+                line["small_batch"] = small_batch(model, meta, device)
                 ref_gpu = reference_cuda(model, meta, envs, device)
                 if ref_gpu is not None:
                     ref_gpu["ours_over_reference"] = value / ref_gpu["value"]
