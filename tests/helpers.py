@@ -74,7 +74,7 @@ def home_q(meta, envs, noise=0.0, seed=1):
 # those copies around the unperturbed oracle is the reference algorithm's own
 # sensitivity to one rounding of its input.
 
-def body_slots(record_length, nb, fp_dtype):
+def body_slots(nb):
     """Indices of the body pose/velocity words (x, q, v, w) of bodies 1..B-1
     in a portable record (header 8, then 16 words per body)."""
     idx = [8 + 16 * b + k for b in range(1, nb) for k in range(13)]
@@ -85,7 +85,7 @@ def perturb_records(records, nb, seed):
     """Copies of `records` [n, L] with every body pose/velocity word moved by
     one ulp, up or down at random (seeded)."""
     out = np.array(records, copy=True)
-    idx = body_slots(out.shape[1], nb, out.dtype)
+    idx = body_slots(nb)
     rng = np.random.default_rng(seed)
     up = rng.random((out.shape[0], idx.size)) < 0.5
     vals = out[:, idx]
