@@ -127,7 +127,9 @@ def _rank(rank, world, port, out):
 
 def test_gradient_all_reduce_two_gloo_ranks():
     world = 2
-    with mp.Manager() as manager:
+    # The manager's server process is spawned too: forking this
+    # multi-threaded process (torch's thread pools) can deadlock the child.
+    with mp.get_context("spawn").Manager() as manager:
         out = manager.dict()
         mp.start_processes(_rank, args=(world, _free_port(), out), nprocs=world, start_method="spawn")
         averaged0, local0, buckets = out[0]
